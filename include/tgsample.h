@@ -1,0 +1,179 @@
+/*
+ * tgsample.h -- C ABI of the B200 batched logits-processing and sampling engine.
+ *
+ * Drop-in boundary for the sarthak-fleet/tinygpt sampling step: the step that
+ * turns the last-position logits of a batch into one token id per row.  Every
+ * entry point takes plain pointers and sizes, returns an int32 status
+ * (TG_OK = 0, negative on error), never throws and never exits the process.
+ * A SwiftPM target binds it through a module map, Python through ctypes.
+ *
+ * Reference interfaces this ABI replaces (paths are inside sarthak-fleet/tinygpt):
+ *   tg_sample        <- TinyGPT.generate sampling block   python_ref/model.py:213-224
+ *                    <- tg_generate sampling tail         wasm/src/model.cpp:489-517
+ *                       (C ABI declared at wasm/src/model.h:39-43)
+ *                    <- sampleToken                       native-mac/Sources/TinyGPTServe/Serve.swift:1483-1506
+ *                    <- repetition penalty + top-k        native-mac/Sources/TinyGPTApp/ModelController.swift:262-304
+ *                    <- LogitsMasker.mask (as a bitmask)  native-mac/Sources/TinyGPTModel/ConstrainedGen.swift:775-837
+ *   tg_spec_verify   <- SpeculativeDecode.stepStochastic  native-mac/Sources/TinyGPT/SpeculativeDecode.swift:121-210
+ *                    <- SpeculativeDecode.step (greedy)   native-mac/Sources/TinyGPT/SpeculativeDecode.swift:41-98
+ *
+ * Memory: all array arguments of tg_sample / tg_spec_verify are DEVICE pointers
+ * on the sampler's device, owned by the caller.  The *_host variants take host
+ * pointers and stage through buffers the handle owns.  Threading: one handle
+ * per device; a handle is not shared between threads without external locking.
+ *
+ * Semantics (bit-exact definition, restated by the CPU oracle):
+ *   y[v]   = logits[v] (bf16 widened exactly to fp32)
+ *   penalties, for each distinct id t in the row's history (count c_t):
+ *            if repetition_penalty > 1: y = y > 0 ? y / rp : y * rp
+ *            if presence or frequency != 0: y = y - (frequency * c_t + presence)
+ *   mask   : state_id >= 0 and bit v of mask_table[state_id] clear -> y = -inf
+ *   greedy : temperature <= 0 -> first index of max y (-1 if every y is -inf)
+ *   s[v]   = y[v] / temperature
+ *   top-k  : 0 < top_k < vocab -> keep s >= k-th largest s (ties kept)
+ *   mass   : q[v] = trunc(tg_exp(s[v] - max s) * 2^44) as uint64 (exact sums)
+ *   top-p  : top_p < 1 -> order survivors by (s desc, id asc), keep the shortest
+ *            prefix whose mass reaches top_p * total mass
+ *   min-p  : min_p > 0 -> keep q >= min(min_p, 1) * 2^44 (the top survivor has q = 2^44)
+ *   draw   : r = trunc(u * S) over the final mass S; first id in INDEX order whose
+ *            inclusive running mass exceeds r.
+ */
+#ifndef TGSAMPLE_H
+#define TGSAMPLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------- */
+#define TG_OK                 0
+#define TG_ERR_INVALID_ARG   -1  /* bad pointer, size, dtype or parameter         */
+#define TG_ERR_CUDA          -2  /* a CUDA runtime call failed                    */
+#define TG_ERR_UNSUPPORTED   -3  /* size beyond a compiled limit                  */
+#define TG_ERR_NO_DEVICE     -4  /* device index not present                      */
+#define TG_ERR_DEVICE_STATUS -5  /* a kernel reported a data error (see below)    */
+
+/* ---- dtypes of the logits --------------------------------------------------- */
+#define TG_DTYPE_F32   0
+#define TG_DTYPE_BF16  1
+
+/* ---- per-row sampling parameters (32 bytes, POD) ---------------------------
+ * temperature <= 0 selects greedy.  top_k <= 0 or >= vocab disables top-k.
+ * top_p >= 1 disables top-p.  min_p <= 0 disables min-p.
+ * repetition_penalty <= 1 disables the CTRL penalty; presence / frequency
+ * penalties of 0 disable them.  flags is reserved and must be 0.            */
+typedef struct tg_row_params {
+  float   temperature;
+  float   top_p;
+  float   min_p;
+  float   repetition_penalty;
+  float   presence_penalty;
+  float   frequency_penalty;
+  int32_t top_k;
+  int32_t flags;
+} tg_row_params;
+
+/* Compiled limits. */
+#define TG_MAX_VOCAB    (1 << 20)  /* ids must fit in 20 bits                  */
+#define TG_MAX_HISTORY  4096       /* history entries per row                  */
+
+typedef struct tg_sampler tg_sampler;
+
+/* Version of this ABI: (major << 16) | minor. */
+int32_t tg_abi_version(void);
+
+/* Message for the last error raised on the calling thread ("" if none). */
+const char* tg_last_error_string(void);
+
+/* Create a sampler bound to CUDA device `device` for rows of `vocab` logits and
+ * at most `max_batch` rows per call.  Allocates the device scratch and the host
+ * staging used by the *_host variants.  Replaces tg_model_create's role as the
+ * owner of sampling state (wasm/src/model.h:21-23); returns TG_OK and *out. */
+int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch,
+                          tg_sampler** out);
+int32_t tg_sampler_destroy(tg_sampler* s);
+
+/* Sample one token per row.  Device pointers:
+ *   logits       [batch, row_stride] of dtype (row_stride >= vocab, in elements)
+ *   params       [batch] tg_row_params
+ *   history      [batch, history_stride] int32 ids (may be NULL if history_len is NULL)
+ *   history_len  [batch] int32, 0..min(history_stride, TG_MAX_HISTORY) (NULL: no history)
+ *   mask_table   [num_states, ceil(vocab/32)] uint32, bit set = token allowed (NULL: no masks)
+ *   state_id     [batch] int32, -1 = unmasked row (NULL: no masks)
+ *   uniforms     [batch] float in [0,1) (ignored for greedy rows)
+ *   out_ids      [batch] int32; -1 where no token is admissible
+ *   out_probs    [batch] float probability of the chosen id under the final
+ *                distribution (1 for greedy rows), may be NULL
+ * Asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream).
+ * Replaces: python_ref/model.py:213-224, wasm/src/model.cpp:489-517,
+ *           Serve.swift:1483-1506, ModelController.swift:262-304. */
+int32_t tg_sample(tg_sampler* s, const void* logits, int32_t dtype,
+                  int64_t row_stride, int32_t batch, const tg_row_params* params,
+                  const int32_t* history, const int32_t* history_len,
+                  int32_t history_stride, const uint32_t* mask_table,
+                  int32_t num_states, const int32_t* state_id,
+                  const float* uniforms, int32_t* out_ids, float* out_probs,
+                  void* stream);
+
+/* Same as tg_sample with every array in HOST memory (pinned or pageable).
+ * Copies the inputs into the handle's device staging, samples, copies the ids
+ * (and probabilities) back and synchronizes before returning.  This is the call
+ * a host-side caller with no device memory of its own makes (the Swift serve
+ * loop's per-token sampleToken, Serve.swift:1483-1506). */
+int32_t tg_sample_host(tg_sampler* s, const void* logits, int32_t dtype,
+                       int64_t row_stride, int32_t batch,
+                       const tg_row_params* params, const int32_t* history,
+                       const int32_t* history_len, int32_t history_stride,
+                       const uint32_t* mask_table, int32_t num_states,
+                       const int32_t* state_id, const float* uniforms,
+                       int32_t* out_ids, float* out_probs);
+
+/* Speculative-decoding verification (rejection sampling), one call per batch.
+ * Device pointers:
+ *   target_logits [batch, K+1, vocab] of dtype (position K is the bonus position)
+ *   draft_logits  [batch, K, vocab] of dtype
+ *   draft_ids     [batch, K] int32 proposals
+ *   temperature   [batch] float; <= 0 selects greedy verification
+ *                 (SpeculativeDecode.swift:41-98), > 0 stochastic with
+ *                 T = max(temperature, 1e-5) (SpeculativeDecode.swift:121-210)
+ *   u_accept      [batch, K] float uniforms for the accept tests
+ *   u_draw        [batch] float uniform for the residual / bonus draw
+ *   out_ids       [batch, K+1] int32: accepted proposals then the final token;
+ *                 entries past out_n are set to -1
+ *   out_n         [batch] int32: number of valid entries (1..K+1)
+ * Accept iff u <= min(1, pT(tok) / max(pD(tok), 1e-10)).  On the first reject
+ * the final token is drawn from max(0, pT - pD) renormalised when its mass
+ * exceeds 1e-10, else from pT; after K accepts it is the bonus drawn from pT at
+ * position K.  Probabilities are q / sum(q) with q the exact masses above. */
+int32_t tg_spec_verify(tg_sampler* s, const void* target_logits,
+                       const void* draft_logits, int32_t dtype, int32_t batch,
+                       int32_t K, const int32_t* draft_ids,
+                       const float* temperature, const float* u_accept,
+                       const float* u_draw, int32_t* out_ids, int32_t* out_n,
+                       void* stream);
+
+/* Device error word of the last completed call on this handle (synchronizes
+ * the handle's device).  Bit 0: a state_id outside [0, num_states);
+ * bit 1: a draft id outside [0, vocab).  Cleared by this call. */
+int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits);
+
+/* Per-handle path counters of tg_sample (diagnostics, the device-side analogue
+ * of the reference's per-token constraint timing, Serve.swift:1489-1491):
+ *   [0] rows finished from the shared-memory candidate list
+ *   [1] rows whose candidate list overflowed      -> full-row path
+ *   [2] rows with fewer than k candidates         -> full-row path
+ *   [3] rows whose top-k threshold fell below the candidate bound -> full-row path
+ *   [4] rows processed by the full-row path (any reason)
+ *   [5] candidates appended (sum over rows)
+ * Copies min(n, TG_PATH_COUNTERS) counters (synchronizes the device); zeroes
+ * them when reset != 0. */
+#define TG_PATH_COUNTERS 8
+int32_t tg_sampler_path_counters(tg_sampler* s, uint64_t* out, int32_t n, int32_t reset);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* TGSAMPLE_H */

@@ -1,0 +1,154 @@
+"""CUDA sampling path vs the oracle: token ids AND probabilities bit-exact
+(the arithmetic is defined op by op, so no tolerance is needed)."""
+import numpy as np
+import pytest
+
+from tinygpt_b200 import workloads as W
+from tests.gpu_helpers import assert_same
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("config,seed", [(1, 0), (1, 1), (2, 0), (2, 1), (3, 0), (3, 1), (4, 0), (4, 1)])
+def test_config_parity_full_size(oracle_mod, sampler_factory, config, seed):
+    w = W.make(config, seed=seed)
+    s = sampler_factory(w["vocab"])
+    assert_same(oracle_mod, s, w, what=f"config {config} seed {seed}")
+
+
+def test_config1_steps(oracle_mod, sampler_factory):
+    """Many steps of the single-row GPT-2 configuration (fresh uniform each step)."""
+    w = W.make(1, seed=3)
+    s = sampler_factory(w["vocab"])
+    g = W.rng(7)
+    for _ in range(50):
+        w["uniforms"] = g.random(1, dtype=np.float32)
+        assert_same(oracle_mod, s, w, what="config1 step")
+
+
+def _base(B, V, seed, dtype="f32", scale=3.0):
+    g = W.rng(seed)
+    x = g.normal(0, scale, size=(B, V)).astype(np.float32)
+    if dtype == "bf16":
+        x = W.to_bf16_bits(x)
+    p = np.zeros(B, W.ROW_PARAMS_DTYPE)
+    p["temperature"] = 0.8
+    p["top_p"] = 1.0
+    return dict(logits=x, params=p, uniforms=g.random(B, dtype=np.float32), vocab=V), g
+
+
+@pytest.mark.parametrize("V", [1, 7, 256, 1000, 3072, 3073, 50257, 128256])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_vocab_sizes_and_modes(oracle_mod, sampler_factory, V, dtype):
+    B = 64
+    w, g = _base(B, V, V * 7 + (dtype == "bf16"), dtype)
+    p = w["params"]
+    p["temperature"] = np.where(np.arange(B) % 4 == 0, 0.0, g.uniform(0.2, 2.0, B))
+    p["top_k"] = g.choice([0, 1, 2, 40, 1024, 2000, V - 1, V, V + 5], size=B)
+    p["top_p"] = g.choice([1.0, 0.9, 0.5, 0.0, 1e-4], size=B)
+    p["min_p"] = g.choice([0.0, 0.0, 0.05, 1.0, 2.0], size=B)
+    assert_same(oracle_mod, sampler_factory(V), w, what=f"V={V} {dtype}")
+
+
+@pytest.mark.parametrize("stride_pad", [1, 3, 8])
+def test_unaligned_row_stride(oracle_mod, sampler_factory, stride_pad):
+    V = 5003
+    for dtype in ("f32", "bf16"):
+        w, g = _base(16, V, stride_pad, dtype)
+        w["params"]["top_k"] = 50
+        assert_same(oracle_mod, sampler_factory(V), w, stride=V + stride_pad, what="stride")
+
+
+def test_sorted_rows_force_full_row_path(oracle_mod, sampler_factory):
+    """Ascending / descending rows defeat the sampled threshold: the candidate
+    list overflows or comes up short and the full-row path must take over."""
+    V = 128256
+    B = 8
+    base = np.linspace(-10, 10, V, dtype=np.float32)
+    x = np.stack([base if b % 2 == 0 else base[::-1].copy() for b in range(B)])
+    p = np.zeros(B, W.ROW_PARAMS_DTYPE)
+    p["temperature"] = [0.0, 0.0, 0.9, 0.9, 0.5, 0.5, 1.0, 1.0]
+    p["top_k"] = [0, 0, 10, 10, 1000, 1000, 3, 3]
+    p["top_p"] = [1.0, 1.0, 0.9, 0.9, 0.5, 0.5, 1.0, 1.0]
+    w = dict(logits=x, params=p, uniforms=W.rng(1).random(B, dtype=np.float32))
+    assert_same(oracle_mod, sampler_factory(V), w, what="sorted")
+
+
+def test_ties_everywhere(oracle_mod, sampler_factory):
+    """Constant rows and two-level rows: top-k keeps all ties, top-p orders
+    ties by id, greedy returns the first maximum."""
+    V = 128256
+    B = 12
+    x = np.zeros((B, V), np.float32)
+    x[4:8, ::3] = 1.0
+    x[8:, :] = W.bf16_bits_to_f32(W.to_bf16_bits(W.rng(3).normal(0, 0.05, size=(4, V)).astype(np.float32)))
+    p = np.zeros(B, W.ROW_PARAMS_DTYPE)
+    p["temperature"] = [0.0, 1.0, 1.0, 1.0] * 3
+    p["top_k"] = [0, 5, 0, 100] * 3
+    p["top_p"] = [1.0, 0.3, 0.5, 0.9] * 3
+    w = dict(logits=x, params=p, uniforms=W.rng(2).random(B, dtype=np.float32))
+    assert_same(oracle_mod, sampler_factory(V), w, what="ties")
+
+
+def test_penalties_edge_cases(oracle_mod, sampler_factory):
+    V = 32000
+    B = 32
+    w, g = _base(B, V, 11, "bf16")
+    p = w["params"]
+    p["temperature"] = np.where(np.arange(B) % 3 == 0, 0.0, 0.9)
+    p["top_k"] = g.choice([0, 20, 500], size=B)
+    p["repetition_penalty"] = g.choice([1.0, 1.3, 0.8, 5.0], size=B)
+    p["presence_penalty"] = g.choice([0.0, 0.5, -1.0], size=B)
+    p["frequency_penalty"] = g.choice([0.0, 0.3, -0.2], size=B)
+    hist = g.integers(-5, V + 5, size=(B, 300)).astype(np.int32)
+    # make the penalised tokens matter: history holds the row's top tokens
+    lg = W.bf16_bits_to_f32(w["logits"])
+    top = np.argsort(-lg, axis=1)[:, :40].astype(np.int32)
+    hist[:, :120] = np.repeat(top, 3, axis=1)
+    w["history"] = hist
+    w["history_len"] = g.integers(0, 301, size=B).astype(np.int32)
+    w["history_len"][0] = 300
+    assert_same(oracle_mod, sampler_factory(V), w, what="penalties")
+
+
+def test_masks_and_bad_states(oracle_mod, sampler_factory):
+    V = 128256
+    B = 16
+    w, g = _base(B, V, 5, "f32")
+    Wd = (V + 31) // 32
+    bits = np.zeros((4, Wd * 32), bool)
+    bits[1, :V] = g.random(V) < 0.001
+    bits[2, 12345] = True
+    bits[3, :V] = True
+    w["mask_table"] = W.pack_mask(bits)
+    w["state_id"] = np.array([0, 1, 2, 3, -1] * 3 + [1], np.int32)
+    w["params"]["temperature"] = np.where(np.arange(B) % 2 == 0, 0.0, 1.0)
+    w["params"]["top_k"] = np.where(np.arange(B) % 4 == 1, 50, 0)
+    s = sampler_factory(V)
+    gi, _ = assert_same(oracle_mod, s, w, what="masks")
+    assert (gi[w["state_id"] == 0] == -1).all()
+    assert (gi[w["state_id"] == 2] == 12345).all()
+    s.device_status()  # clear
+    w["state_id"] = np.array([7] + [0] * (B - 1), np.int32)
+    gi, _ = assert_same(oracle_mod, s, w, what="bad state")
+    assert gi[0] == -1 and s.device_status() & 1
+
+
+def test_uniform_edges(oracle_mod, sampler_factory):
+    V = 128256
+    B = 8
+    w, g = _base(B, V, 9, "bf16")
+    w["params"]["top_k"] = 100
+    w["uniforms"] = np.array([0.0, np.nextafter(1.0, 0.0), np.nan, -1.0, 1.0, 0.5, 1e-30, 0.999],
+                             np.float32)
+    assert_same(oracle_mod, sampler_factory(V), w, what="uniforms")
+
+
+def test_host_entry_point_matches_device_entry_point(oracle_mod, sampler_factory):
+    w = W.make(4, seed=5, batch=64)
+    s = sampler_factory(w["vocab"])
+    hi, hp = s.sample_host(w["logits"], w["params"], history=w["history"],
+                           history_len=w["history_len"], uniforms=w["uniforms"], want_probs=True)
+    oi, op = oracle_mod.sample(w["logits"], w["params"], w["history"], w["history_len"], None,
+                               None, w["uniforms"])
+    assert np.array_equal(hi, oi) and np.array_equal(hp.view(np.uint32), op.view(np.uint32))

@@ -1,0 +1,270 @@
+// tg_block.cuh -- CTA-wide building blocks: reductions, a warp-aggregated
+// candidate append, and a weighted MSB-first radix search.
+#pragma once
+
+#include "tg_common.cuh"
+
+namespace tg {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+struct __align__(16) BlockScratch {
+  unsigned long long hmass[256];
+  unsigned int hcnt[256];
+  unsigned int hfine[256];  // elements whose key has non-zero low 16 bits (kEarly16)
+  unsigned long long red_u64[32];
+  float red_f[32];
+  int red_i[32];
+  unsigned long long sel_before;
+  unsigned long long sel_mass;
+  unsigned int sel_bin;
+  unsigned int sel_cbefore;
+  unsigned int sel_cnt;
+  int cand_count;
+};
+
+template <int NT>
+__device__ __forceinline__ float block_max(float v, BlockScratch& sm) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+  if ((threadIdx.x & 31) == 0) sm.red_f[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = sm.red_f[0];
+#pragma unroll
+  for (int i = 1; i < NT / 32; i++) r = fmaxf(r, sm.red_f[i]);
+  __syncthreads();
+  return r;
+}
+
+template <int NT>
+__device__ __forceinline__ unsigned long long block_sum(unsigned long long v, BlockScratch& sm) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  if ((threadIdx.x & 31) == 0) sm.red_u64[threadIdx.x >> 5] = v;
+  __syncthreads();
+  unsigned long long r = 0;
+#pragma unroll
+  for (int i = 0; i < NT / 32; i++) r += sm.red_u64[i];
+  __syncthreads();
+  return r;
+}
+
+// Max y, then the smallest id holding it.  Returns via references.
+template <int NT>
+__device__ __forceinline__ void block_argmax(float& y, int& id, BlockScratch& sm) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const float oy = __shfl_xor_sync(kFull, y, o);
+    const int oi = __shfl_xor_sync(kFull, id, o);
+    if (oy > y || (oy == y && oi < id)) { y = oy; id = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm.red_f[threadIdx.x >> 5] = y;
+    sm.red_i[threadIdx.x >> 5] = id;
+  }
+  __syncthreads();
+  y = sm.red_f[0];
+  id = sm.red_i[0];
+#pragma unroll
+  for (int i = 1; i < NT / 32; i++) {
+    const float oy = sm.red_f[i];
+    const int oi = sm.red_i[i];
+    if (oy > y || (oy == y && oi < id)) { y = oy; id = oi; }
+  }
+  __syncthreads();
+}
+
+// Exclusive prefix sum of one u64 per thread in thread order; also the total.
+template <int NT>
+__device__ __forceinline__ unsigned long long block_excl_scan(unsigned long long v,
+                                                              unsigned long long& total,
+                                                              BlockScratch& sm) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  unsigned long long incl = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long n = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) sm.red_u64[w] = incl;
+  __syncthreads();
+  unsigned long long before = 0;
+  total = 0;
+#pragma unroll
+  for (int i = 0; i < NT / 32; i++) {
+    const unsigned long long s = sm.red_u64[i];
+    if (i < w) before += s;
+    total += s;
+  }
+  __syncthreads();
+  return before + incl - v;
+}
+
+// Append the elements flagged in `hits` (bit e = x[e], token e0+e) to the
+// candidate arrays.  Must be called by all 32 lanes of the warp.
+template <int N, int CMAX>
+__device__ __forceinline__ void warp_append(uint32_t hits, const float* x, int e0, float* cy,
+                                            int* cid, int* counter) {
+  const int lane = threadIdx.x & 31;
+  const int cnt = __popc(hits);
+  int incl = cnt;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += n;
+  }
+  const int total = __shfl_sync(kFull, incl, 31);
+  if (total == 0) return;
+  int base = 0;
+  if (lane == 31) base = atomicAdd(counter, total);
+  base = __shfl_sync(kFull, base, 31);
+  int pos = base + incl - cnt;
+#pragma unroll
+  for (int e = 0; e < N; e++) {
+    if ((hits >> e) & 1u) {
+      if (pos < CMAX) { cy[pos] = x[e]; cid[pos] = e0 + e; }
+      pos++;
+    }
+  }
+}
+
+// Histogram update aggregated over the lanes of a warp that hit the same bin
+// (one shared atomic per distinct bin per warp instead of one per lane).
+template <bool kMass>
+__device__ __forceinline__ void hist_add(BlockScratch& sm, uint32_t d, unsigned long long w) {
+  const unsigned act = __activemask();
+  const unsigned peers = __match_any_sync(act, d);
+  if (kMass) {  // sum of w over the peers, in three 22-bit slices (no u32 overflow)
+    const unsigned lo = __reduce_add_sync(peers, static_cast<unsigned>(w & 0x3fffffull));
+    const unsigned mid = __reduce_add_sync(peers, static_cast<unsigned>((w >> 22) & 0x3fffffull));
+    const unsigned hi = __reduce_add_sync(peers, static_cast<unsigned>(w >> 44));
+    w = static_cast<unsigned long long>(lo) + (static_cast<unsigned long long>(mid) << 22) +
+        (static_cast<unsigned long long>(hi) << 44);
+  }
+  if ((threadIdx.x & 31) == __ffs(peers) - 1) {
+    atomicAdd(&sm.hcnt[d], static_cast<unsigned>(__popc(peers)));
+    if (kMass) atomicAdd(&sm.hmass[d], w);
+  }
+}
+
+// Weighted MSB-first radix search over the elements a Source yields.
+//
+// keyw(id, y, key, w) -> bool: whether the element takes part, its key
+// (nbits wide) and weight.  Digits are scanned in descending key order when
+// kDesc, ascending otherwise, accumulating (mass, count) from the keys already
+// passed; the result is the key of the element at which reached(mass, count)
+// first holds, including that key's whole bin.  Outputs: the key, the mass and
+// count strictly before it in scan order, and the mass and count of elements
+// with exactly that key.
+// Rounds stop once the bits above `min_shift` are resolved (the low bits of
+// key_out are then zero: the search is approximate below that resolution).
+// kEarly16: stop after the top 16 bits when no element of the selected bin has
+// non-zero low 16 bits (all of them then share the key exactly -- the common
+// case for bf16 logits).
+template <int NT, bool kDesc, bool kMass, class Src, class KeyW, class Reached, bool kEarly16 = false>
+__device__ void radix_find(const Src& src, int nbits, KeyW keyw, Reached reached,
+                           BlockScratch& sm, uint32_t& key_out, unsigned long long& before_out,
+                           unsigned int& cbefore_out, unsigned int& cnt_out,
+                           unsigned long long& mass_out, int min_shift = 0) {
+  uint32_t prefix = 0, pmask = 0;
+  unsigned long long before = 0;
+  unsigned int cbefore = 0;
+  unsigned int bcnt = 0;
+  unsigned long long bmass = 0;
+  int shift = nbits;
+  while (shift > min_shift) {
+    const int width = shift >= 8 ? 8 : shift;
+    shift -= width;
+    const uint32_t dmask = (1u << width) - 1u;
+    const bool fine_round = kEarly16 && shift == 16;
+    for (int i = threadIdx.x; i < 256; i += NT) {
+      sm.hmass[i] = 0ull;
+      sm.hcnt[i] = 0u;
+      if (fine_round) sm.hfine[i] = 0u;
+    }
+    __syncthreads();
+    src.for_each([&](int id, float y) {
+      uint32_t key;
+      unsigned long long w;
+      if (!keyw(id, y, key, w)) return;
+      if ((key & pmask) != prefix) return;
+      hist_add<kMass>(sm, (key >> shift) & dmask, w);
+      if (fine_round && (key & 0xffffu)) atomicAdd(&sm.hfine[(key >> shift) & dmask], 1u);
+    });
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      const int nb = 1 << width;
+      const int per = (nb + 31) >> 5;
+      unsigned long long lm = 0;
+      unsigned int lc = 0;
+      for (int q = 0; q < per; q++) {
+        const int p = lane * per + q;
+        if (p < nb) {
+          const int bin = kDesc ? nb - 1 - p : p;
+          lm += kMass ? sm.hmass[bin] : 0ull;
+          lc += sm.hcnt[bin];
+        }
+      }
+      unsigned long long em = lm;
+      unsigned int ec = lc;
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long tm = __shfl_up_sync(kFull, em, o);
+        const unsigned int tc = __shfl_up_sync(kFull, ec, o);
+        if (lane >= o) { em += tm; ec += tc; }
+      }
+      em -= lm;
+      ec -= lc;
+      unsigned long long cm = before + em;
+      unsigned int cc = cbefore + ec;
+      int found = -1, last = -1;
+      unsigned long long fb = 0, lb = 0;
+      unsigned int fcb = 0, lcb = 0;
+      for (int q = 0; q < per; q++) {
+        const int p = lane * per + q;
+        if (p < nb) {
+          const int bin = kDesc ? nb - 1 - p : p;
+          const unsigned long long m = kMass ? sm.hmass[bin] : 0ull;
+          const unsigned int c = sm.hcnt[bin];
+          if (c > 0) {
+            if (found < 0 && reached(cm + m, cc + c)) { found = bin; fb = cm; fcb = cc; }
+            last = bin; lb = cm; lcb = cc;
+          }
+          cm += m;
+          cc += c;
+        }
+      }
+      const unsigned bal = __ballot_sync(kFull, found >= 0);
+      if (bal) {
+        if (lane == __ffs(bal) - 1) {
+          sm.sel_bin = found; sm.sel_before = fb; sm.sel_cbefore = fcb;
+        }
+      } else {  // target beyond the total (defensive): take the last non-empty bin
+        const unsigned bl = __ballot_sync(kFull, last >= 0);
+        if (bl && lane == 31 - __clz(bl)) {
+          sm.sel_bin = last; sm.sel_before = lb; sm.sel_cbefore = lcb;
+        } else if (!bl && lane == 0) {
+          sm.sel_bin = 0; sm.sel_before = before; sm.sel_cbefore = cbefore;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        sm.sel_cnt = sm.hcnt[sm.sel_bin];
+        sm.sel_mass = kMass ? sm.hmass[sm.sel_bin] : 0ull;
+      }
+    }
+    __syncthreads();
+    const uint32_t bin = sm.sel_bin;
+    before = sm.sel_before;
+    cbefore = sm.sel_cbefore;
+    bcnt = sm.sel_cnt;
+    bmass = sm.sel_mass;
+    prefix |= bin << shift;
+    pmask |= dmask << shift;
+    const bool exact = fine_round && sm.hfine[bin] == 0u;
+    __syncthreads();
+    if (exact) break;
+  }
+  key_out = prefix;
+  before_out = before;
+  cbefore_out = cbefore;
+  cnt_out = bcnt;
+  mass_out = bmass;
+}
+
+}  // namespace tg

@@ -1,0 +1,779 @@
+// tg_sample.cuh -- the fused sampling kernel: penalties + grammar mask +
+// temperature + top-k + top-p / min-p + inverse-CDF draw, one CTA per row.
+//
+// Reference path (sarthak-fleet/tinygpt): python_ref/model.py:213-224,
+// wasm/src/model.cpp:489-517, ModelController.swift:262-304,
+// ConstrainedGen.swift:775-837, Serve.swift:1483-1506.
+//
+// Structure of one row (one CTA):
+//   (a) penalty-and-mask: history ids go into a shared-memory hash (id -> count
+//       -> penalised value); the mask row is gathered by state id and applied
+//       to every 128-bit vector as it streams in.
+//   (c) top-k prefilter: a sample of the row (the first vectors of every
+//       thread) gives a threshold theta expected to pass ~1.5k+64 elements;
+//       the single HBM pass appends every element >= theta to a shared-memory
+//       candidate list (warp-aggregated, ballot-based).  The pass is one
+//       128-bit load plus a vector max and a compare per 16 bytes.
+//       The exact k-th value is then a radix select over the candidates.  If
+//       the list overflowed or holds fewer than k elements >= theta, the row
+//       is redone by the full-row path below (same stages, over global memory).
+//   (b) softmax as exact fixed-point masses q = trunc(tg_exp(s - max) * 2^44).
+//   (d) top-p: a mass-weighted radix search in (s desc, id asc) order; min-p:
+//       a threshold on q.
+//   (e) draw: r = trunc(u * S); a mass-weighted radix search over ids in
+//       ascending order finds the first id whose running mass exceeds r.
+#pragma once
+
+#include "../../include/tgsample.h"
+#include "tg_block.cuh"
+
+namespace tg {
+
+constexpr int kSampleNT = 256;   // threads per CTA
+constexpr int kCandMax = 3072;   // candidate list capacity
+constexpr int kFastMaxK = 1024;  // largest top-k served by the candidate path
+constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold sample
+#ifndef TG_UNROLL
+#define TG_UNROLL 4
+#endif
+constexpr int kUnroll = TG_UNROLL;  // 128-bit loads in flight per thread
+constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) before the full row
+constexpr int kMinCtasPerSm = 4; // occupancy target (caps registers at 64)
+
+struct SampleArgs {
+  const void* logits;
+  int64_t row_stride;
+  int32_t vocab;
+  int32_t batch;
+  const tg_row_params* params;
+  const int32_t* history;
+  const int32_t* history_len;
+  int32_t history_stride;
+  int32_t hist_cap;   // min(history_stride, TG_MAX_HISTORY), 0 if no history
+  int32_t ht_log2;    // log2 of the hash size (0 if no history)
+  const uint32_t* mask_table;
+  int32_t num_states;
+  int32_t mask_words;
+  const int32_t* state_id;
+  const float* uniforms;
+  int32_t* out_ids;
+  float* out_probs;
+  uint32_t* status;
+  unsigned long long* counters;  // TG_PATH_* counters
+};
+
+// History hash in shared memory: key = token id (-1 empty); val = count, then
+// the penalised value's float bits.  A 4096-bit Bloom word set filters lookups.
+struct Hist {
+  int* key;
+  int* val;
+  uint32_t* bloom;
+  int mask;
+  int log2;
+  int active;
+  __device__ __forceinline__ int slot0(int id) const {
+    return static_cast<int>((static_cast<uint32_t>(id) * 0x9E3779B1u) >> (32 - log2));
+  }
+  __device__ __forceinline__ bool find(int id, float& y) const {
+    if (!active) return false;
+    const uint32_t h = (static_cast<uint32_t>(id) * 0x85EBCA77u) >> 20;
+    if (!((bloom[h >> 5] >> (h & 31)) & 1u)) return false;
+    int s = slot0(id);
+    for (;;) {
+      const int k = key[s];
+      if (k == id) { y = __int_as_float(val[s]); return true; }
+      if (k == -1) return false;
+      s = (s + 1) & mask;
+    }
+  }
+};
+
+// Every element of the row, recomputed from global memory (L2 after the first
+// pass): 128-bit loads over the aligned middle, scalars for head and tail.
+template <int DT>
+struct GlobalSrc {
+  const char* row;
+  int V, head, nvec, tail0;
+  const uint32_t* mask;
+  Hist hist;
+  template <class F>
+  __device__ __forceinline__ void for_each(F&& f) const {
+    using E = Elt<DT>;
+    constexpr int EPV = E::kEPV;
+    auto one = [&](int v, float x) {
+      float y;
+      if (!hist.find(v, y)) y = (mask && !mask_allows(mask, v)) ? neg_inf() : x;
+      f(v, y);
+    };
+    const int t = threadIdx.x;
+    if (t < head) one(t, E::load(row, t));
+    if (t < V - tail0) one(tail0 + t, E::load(row, tail0 + t));
+    const uint4* vrow = reinterpret_cast<const uint4*>(row + head * E::kSize);
+    for (int j = t; j < nvec; j += kSampleNT) {
+      float x[EPV];
+      E::unpack(__ldg(vrow + j), x);
+      const int e0 = head + j * EPV;
+      const uint32_t bits = mask ? mask_bits(mask, e0, EPV) : 0xffu;
+#pragma unroll
+      for (int e = 0; e < EPV; e++) {
+        float y;
+        if (!hist.find(e0 + e, y)) y = ((bits >> e) & 1u) ? x[e] : neg_inf();
+        f(e0 + e, y);
+      }
+    }
+  }
+};
+
+struct SmemSrc {
+  const float* y;
+  const int* id;
+  int n;
+  float theta;
+  template <class F>
+  __device__ __forceinline__ void for_each(F&& f) const {
+    for (int i = threadIdx.x; i < n; i += kSampleNT) {
+      const float v = y[i];
+      if (v >= theta) f(id[i], v);
+    }
+  }
+};
+
+template <int N>
+struct RegSrc {  // N values per thread, held in registers
+  const float* v;
+  template <class F>
+  __device__ __forceinline__ void for_each(F&& f) const {
+#pragma unroll
+    for (int i = 0; i < N; i++) f(threadIdx.x, v[i]);
+  }
+};
+
+template <class Src>
+__device__ __forceinline__ unsigned int block_count_if(const Src& src, float thr, BlockScratch& sm) {
+  unsigned long long c = 0;
+  src.for_each([&](int, float y) { c += (y >= thr) ? 1ull : 0ull; });
+  return static_cast<unsigned int>(block_sum<kSampleNT>(c, sm));
+}
+
+// Stages (b)-(e) over a source.  Returns false (and writes nothing) when the
+// source is a candidate list that turns out to miss an element the top-k
+// threshold keeps; the caller then reruns the row over the full row.
+template <class Src>
+__device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float u,
+                           bool check_theta, float theta, BlockScratch& sm, int& out_id,
+                           float& out_prob) {
+  if (!(p.temperature > 0.0f)) {  // greedy: first index of the maximum
+    float y = neg_inf();
+    int id = 0x7fffffff;
+    src.for_each([&](int i, float v) {
+      if (v > y || (v == y && i < id)) { y = v; id = i; }
+    });
+    block_argmax<kSampleNT>(y, id, sm);
+    if (y == neg_inf()) { out_id = -1; out_prob = 0.0f; }
+    else { out_id = id; out_prob = 1.0f; }
+    return true;
+  }
+  const float T = p.temperature;
+  const bool topk = p.top_k > 0 && p.top_k < V;
+  float sk = neg_inf();
+  if (topk) {
+    uint32_t kkey; unsigned long long b0, m0; unsigned int c0, n0;
+    const unsigned int k = static_cast<unsigned int>(p.top_k);
+    radix_find<kSampleNT, true, false>(
+        src, 32,
+        [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; },
+        [&](unsigned long long, unsigned int c) { return c >= k; }, sm, kkey, b0, c0, n0, m0);
+    const float kth = key2f(kkey);
+    sk = __fdiv_rn(kth, T);
+    if (check_theta && theta > neg_inf()) {
+      // every element below theta is absent; none of them may reach sk
+      const float bk = key2f(fkey(theta) - 1u);  // next float below theta
+      if (__fdiv_rn(bk, T) >= sk) return false;
+    }
+  }
+  float ymax = neg_inf();
+  src.for_each([&](int, float y) { ymax = fmaxf(ymax, y); });
+  ymax = block_max<kSampleNT>(ymax, sm);
+  if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
+  const float smax = __fdiv_rn(ymax, T);
+
+  auto inA = [&](float y, float& s) {
+    if (!(y > neg_inf())) return false;
+    s = __fdiv_rn(y, T);
+    return !topk || s >= sk;
+  };
+
+  unsigned long long Q = 0;
+  src.for_each([&](int, float y) {
+    float s;
+    if (inA(y, s)) Q += qmass(__fsub_rn(s, smax));
+  });
+  Q = block_sum<kSampleNT>(Q, sm);
+
+  // (d) top-p: last element (cut_key, cut_id) of the shortest (s desc, id asc)
+  // prefix whose mass reaches top_p * Q.
+  const bool toppon = p.top_p < 1.0f;
+  uint32_t cut_key = 0;
+  int cut_id = 0x7fffffff;
+  if (toppon) {
+    const double tau = __dmul_rn(static_cast<double>(p.top_p), __ull2double_rn(Q));
+    unsigned long long above = 0, qt = 0;
+    unsigned int nties = 0;
+    unsigned long long jstar = 1;
+    if (!(tau > 0.0)) {
+      cut_key = fkey(smax);
+      unsigned long long c = 0;
+      src.for_each([&](int, float y) {
+        float s;
+        if (inA(y, s) && fkey(s) == cut_key) c++;
+      });
+      nties = static_cast<unsigned int>(block_sum<kSampleNT>(c, sm));
+    } else {
+      unsigned int cb;
+      radix_find<kSampleNT, true, true>(
+          src, 32,
+          [&](int, float y, uint32_t& key, unsigned long long& w) {
+            float s;
+            if (!inA(y, s)) return false;
+            key = fkey(s);
+            w = qmass(__fsub_rn(s, smax));
+            return true;
+          },
+          [&](unsigned long long m, unsigned int) { return __ull2double_rn(m) >= tau; }, sm,
+          cut_key, above, cb, nties, qt);
+      qt = qmass(__fsub_rn(key2f(cut_key), smax));
+      if (qt > 0) {
+        const double need = tau - __ull2double_rn(above);
+        if (need > 0.0) {
+          const double est = ceil(__ddiv_rn(need, __ull2double_rn(qt)));
+          jstar = est < 1.0 ? 1ull : static_cast<unsigned long long>(est);
+        }
+        if (jstar > nties) jstar = nties;
+        while (jstar > 1 && __ull2double_rn(above + (jstar - 1) * qt) >= tau) jstar--;
+        while (jstar < nties && __ull2double_rn(above + jstar * qt) < tau) jstar++;
+      }
+    }
+    if (jstar < nties) {
+      uint32_t idkey; unsigned long long b1, m1; unsigned int c1, n1;
+      const unsigned int js = static_cast<unsigned int>(jstar);
+      radix_find<kSampleNT, false, false>(
+          src, 20,
+          [&](int id, float y, uint32_t& key, unsigned long long& w) {
+            float s;
+            if (!inA(y, s) || fkey(s) != cut_key) return false;
+            key = static_cast<uint32_t>(id);
+            w = 0;
+            return true;
+          },
+          [&](unsigned long long, unsigned int c) { return c >= js; }, sm, idkey, b1, c1, n1, m1);
+      cut_id = static_cast<int>(idkey);
+    }
+  }
+  const bool minpon = p.min_p > 0.0f;
+  const double minq = __dmul_rn(static_cast<double>(fminf(p.min_p, 1.0f)),
+                                static_cast<double>(kMassScale));
+  auto inF = [&](int id, float y, unsigned long long& q) {
+    float s;
+    if (!inA(y, s)) return false;
+    if (toppon) {
+      const uint32_t k = fkey(s);
+      if (k < cut_key || (k == cut_key && id > cut_id)) return false;
+    }
+    q = qmass(__fsub_rn(s, smax));
+    return !minpon || __ull2double_rn(q) >= minq;
+  };
+
+  unsigned long long S = 0;
+  src.for_each([&](int id, float y) {
+    unsigned long long q;
+    if (inF(id, y, q)) S += q;
+  });
+  S = block_sum<kSampleNT>(S, sm);
+  const unsigned long long r = draw_point(u, S);
+
+  uint32_t pick; unsigned long long b2, qpick; unsigned int c2, n2;
+  radix_find<kSampleNT, false, true>(
+      src, 20,
+      [&](int id, float y, uint32_t& key, unsigned long long& w) {
+        if (!inF(id, y, w)) return false;
+        key = static_cast<uint32_t>(id);
+        return true;
+      },
+      [&](unsigned long long m, unsigned int) { return m > r; }, sm, pick, b2, c2, n2, qpick);
+  out_id = static_cast<int>(pick);
+  out_prob = __double2float_rn(__ddiv_rn(__ull2double_rn(qpick), __ull2double_rn(S)));
+  return true;
+}
+
+// Survivors of the candidate path after compaction: slot i holds the tempered
+// logit s (cand_y), the id (cand_id, -1 when dropped) and e = tg_exp(s - smax)
+// (cand_e), so q = trunc(e * 2^44) needs no division or exponential.
+struct ASrc {
+  const float* s;
+  const int* id;
+  int n;
+  template <class F>
+  __device__ __forceinline__ void for_each(F&& f) const {
+    for (int i = threadIdx.x; i < n; i += kSampleNT)
+      if (id[i] >= 0) f(i, s[i]);
+  }
+};
+
+__device__ __forceinline__ unsigned long long mass_of_e(float e) {
+  return __float2ull_rz(__fmul_rn(e, kMassScale));
+}
+
+// Stages (b)-(e) over the shared-memory candidate list (all elements >= theta
+// of the row).  Same results as finish_row; returns false when an element
+// below theta could survive top-k (the caller retries with a lower theta).
+__device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
+                             const tg_row_params& p, int V, float u, BlockScratch& sm,
+                             int& out_id, float& out_prob) {
+  SmemSrc src{cy, cid, n, theta};
+  if (!(p.temperature > 0.0f)) return finish_row(src, p, V, u, false, theta, sm, out_id, out_prob);
+  const float T = p.temperature;
+  const bool topk = p.top_k > 0 && p.top_k < V;
+  float sk = neg_inf();
+  if (topk) {
+    uint32_t kkey; unsigned long long b0, m0; unsigned int c0, n0;
+    const unsigned int k = static_cast<unsigned int>(p.top_k);
+    auto kw = [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; };
+    auto rc = [&](unsigned long long, unsigned int c) { return c >= k; };
+    radix_find<kSampleNT, true, false, SmemSrc, decltype(kw), decltype(rc), true>(
+        src, 32, kw, rc, sm, kkey, b0, c0, n0, m0);
+    sk = __fdiv_rn(key2f(kkey), T);
+    if (theta > neg_inf() && __fdiv_rn(key2f(fkey(theta) - 1u), T) >= sk) return false;
+  }
+  float ymax = neg_inf();
+  src.for_each([&](int, float y) { ymax = fmaxf(ymax, y); });
+  ymax = block_max<kSampleNT>(ymax, sm);
+  if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
+  const float smax = __fdiv_rn(ymax, T);
+
+  // compaction: s, e in place; ids of dropped slots set to -1
+  unsigned long long Q = 0;
+  for (int i = threadIdx.x; i < n; i += kSampleNT) {
+    const float y = cy[i];
+    bool keep = y >= theta && y > neg_inf();
+    float sv = 0.0f, e = 0.0f;
+    if (keep) {
+      sv = __fdiv_rn(y, T);
+      keep = !topk || sv >= sk;
+    }
+    if (keep) {
+      const float d = __fsub_rn(sv, smax);
+      e = d >= -32.0f ? tg_exp(d) : 0.0f;
+      Q += mass_of_e(e);
+      cy[i] = sv;
+      ce[i] = e;
+    } else {
+      cid[i] = -1;
+    }
+  }
+  Q = block_sum<kSampleNT>(Q, sm);  // (its barrier also publishes the compaction)
+  ASrc as{cy, cid, n};
+
+  const bool toppon = p.top_p < 1.0f;
+  uint32_t cut_key = 0;
+  int cut_id = 0x7fffffff;
+  if (toppon) {
+    const double tau = __dmul_rn(static_cast<double>(p.top_p), __ull2double_rn(Q));
+    unsigned long long above = 0, qt = 0;
+    unsigned int nties = 0;
+    unsigned long long jstar = 1;
+    if (!(tau > 0.0)) {
+      cut_key = fkey(smax);
+      unsigned long long c = 0;
+      as.for_each([&](int, float sv) { c += (fkey(sv) == cut_key) ? 1ull : 0ull; });
+      nties = static_cast<unsigned int>(block_sum<kSampleNT>(c, sm));
+    } else {
+      unsigned int cb;
+      radix_find<kSampleNT, true, true>(
+          as, 32,
+          [&](int i, float sv, uint32_t& key, unsigned long long& w) {
+            key = fkey(sv);
+            w = mass_of_e(ce[i]);
+            return true;
+          },
+          [&](unsigned long long m, unsigned int) { return __ull2double_rn(m) >= tau; }, sm,
+          cut_key, above, cb, nties, qt);
+      qt = qmass(__fsub_rn(key2f(cut_key), smax));
+      if (qt > 0) {
+        const double need = tau - __ull2double_rn(above);
+        if (need > 0.0) {
+          const double est = ceil(__ddiv_rn(need, __ull2double_rn(qt)));
+          jstar = est < 1.0 ? 1ull : static_cast<unsigned long long>(est);
+        }
+        if (jstar > nties) jstar = nties;
+        while (jstar > 1 && __ull2double_rn(above + (jstar - 1) * qt) >= tau) jstar--;
+        while (jstar < nties && __ull2double_rn(above + jstar * qt) < tau) jstar++;
+      }
+    }
+    if (jstar < nties) {
+      uint32_t idkey; unsigned long long b1, m1; unsigned int c1, n1;
+      const unsigned int js = static_cast<unsigned int>(jstar);
+      radix_find<kSampleNT, false, false>(
+          as, 20,
+          [&](int i, float sv, uint32_t& key, unsigned long long& w) {
+            if (fkey(sv) != cut_key) return false;
+            key = static_cast<uint32_t>(cid[i]);
+            w = 0;
+            return true;
+          },
+          [&](unsigned long long, unsigned int c) { return c >= js; }, sm, idkey, b1, c1, n1, m1);
+      cut_id = static_cast<int>(idkey);
+    }
+  }
+  const bool minpon = p.min_p > 0.0f;
+  const double minq = __dmul_rn(static_cast<double>(fminf(p.min_p, 1.0f)),
+                                static_cast<double>(kMassScale));
+  // final set: drop slots outside top-p / min-p
+  unsigned long long S = 0;
+  for (int i = threadIdx.x; i < n; i += kSampleNT) {
+    const int id = cid[i];
+    if (id < 0) continue;
+    const unsigned long long q = mass_of_e(ce[i]);
+    bool keep = true;
+    if (toppon) {
+      const uint32_t k = fkey(cy[i]);
+      keep = k > cut_key || (k == cut_key && id <= cut_id);
+    }
+    if (keep && minpon) keep = __ull2double_rn(q) >= minq;
+    if (keep) S += q;
+    else cid[i] = -1;
+  }
+  S = block_sum<kSampleNT>(S, sm);
+  const unsigned long long r = draw_point(u, S);
+  uint32_t pick; unsigned long long b2, qpick; unsigned int c2, n2;
+  radix_find<kSampleNT, false, true>(
+      as, 20,
+      [&](int i, float, uint32_t& key, unsigned long long& w) {
+        key = static_cast<uint32_t>(cid[i]);
+        w = mass_of_e(ce[i]);
+        return true;
+      },
+      [&](unsigned long long m, unsigned int) { return m > r; }, sm, pick, b2, c2, n2, qpick);
+  out_id = static_cast<int>(pick);
+  out_prob = __double2float_rn(__ddiv_rn(__ull2double_rn(qpick), __ull2double_rn(S)));
+  return true;
+}
+
+// Threshold search on the per-vector maxima of the sample: the rk-th largest,
+// resolved to 16 bits (a lower bound of the exact value).
+template <int N>
+__device__ __forceinline__ float sample_threshold(const float* vmax, unsigned int rk, BlockScratch& sm) {
+  uint32_t tk; unsigned long long b0, m0; unsigned int c0, n0;
+  radix_find<kSampleNT, true, false>(
+      RegSrc<N>{vmax}, 32,
+      [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; },
+      [&](unsigned long long, unsigned int c) { return c >= rk; }, sm, tk, b0, c0, n0, m0, 16);
+  return key2f(tk);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(SampleArgs a) {
+  using E = Elt<DT>;
+  constexpr int EPV = E::kEPV;
+  constexpr int SV = kSampleVecs;
+  extern __shared__ __align__(16) unsigned char dyn[];
+  __shared__ BlockScratch sm;
+  __shared__ uint32_t bloom[128];
+
+  const int b = blockIdx.x;
+  const int t = threadIdx.x;
+  const int V = a.vocab;
+  float* cand_y = reinterpret_cast<float*>(dyn);
+  int* cand_id = reinterpret_cast<int*>(dyn + kCandMax * 4);
+  float* cand_e = reinterpret_cast<float*>(dyn + kCandMax * 8);
+  int* hkey = reinterpret_cast<int*>(dyn + kCandMax * 12);
+  const int ht = a.ht_log2 ? (1 << a.ht_log2) : 0;
+  int* hval = hkey + ht;
+
+  const tg_row_params p = a.params[b];
+  const char* row = reinterpret_cast<const char*>(a.logits) + b * a.row_stride * E::kSize;
+  const float u = a.uniforms ? a.uniforms[b] : 0.0f;
+
+  const uint32_t* mask = nullptr;
+  if (a.mask_table && a.state_id) {
+    const int sid = a.state_id[b];
+    if (sid >= a.num_states) {
+      if (t == 0) {
+        a.out_ids[b] = -1;
+        if (a.out_probs) a.out_probs[b] = 0.0f;
+        atomicOr(a.status, 1u);
+      }
+      return;
+    }
+    if (sid >= 0) mask = a.mask_table + static_cast<int64_t>(sid) * a.mask_words;
+  }
+
+  // row geometry: scalar head up to the first 16-byte boundary, vectors, tail
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
+  int head = static_cast<int>(((16u - (addr & 15u)) & 15u) / E::kSize);
+  if (head > V) head = V;
+  const int nvec = (V - head) / EPV;
+  const int tail0 = head + nvec * EPV;
+  const uint4* vrow = reinterpret_cast<const uint4*>(row + head * E::kSize);
+
+  int hlen = 0;
+  if (a.history_len && a.history && a.hist_cap > 0) {
+    hlen = a.history_len[b];
+    hlen = hlen < 0 ? 0 : (hlen > a.hist_cap ? a.hist_cap : hlen);
+  }
+  const bool rep_on = p.repetition_penalty > 1.0f;
+  const bool pf_on = p.presence_penalty != 0.0f || p.frequency_penalty != 0.0f;
+  Hist hist{hkey, hval, bloom, ht - 1, a.ht_log2, 0};
+  const bool need_hist = hlen > 0 && (rep_on || pf_on);
+
+  // (a) history -> shared hash of penalised values (raw values read from L2
+  // when this runs after the streaming pass)
+  // build_hist(th): penalised values of the distinct history ids; ids whose
+  // penalised value reaches th while the raw one did not are appended to the
+  // candidate list (th = +inf appends nothing).
+  auto build_hist = [&](float th) {
+    if (!need_hist || hist.active) return;
+    for (int i = t; i < ht; i += kSampleNT) { hkey[i] = -1; hval[i] = 0; }
+    for (int i = t; i < 128; i += kSampleNT) bloom[i] = 0u;
+    __syncthreads();
+    const int32_t* h = a.history + static_cast<int64_t>(b) * a.history_stride;
+    for (int i = t; i < hlen; i += kSampleNT) {
+      const int id = h[i];
+      if (id < 0 || id >= V) continue;
+      int s = hist.slot0(id);
+      for (;;) {
+        const int old = atomicCAS(&hkey[s], -1, id);
+        if (old == -1 || old == id) { atomicAdd(&hval[s], 1); break; }
+        s = (s + 1) & (ht - 1);
+      }
+    }
+    __syncthreads();
+    for (int s = t; s < ht; s += kSampleNT) {
+      const int id = hkey[s];
+      if (id < 0) continue;
+      const int c = hval[s];
+      float raw = E::load(row, id);
+      if (mask && !mask_allows(mask, id)) raw = neg_inf();
+      float y = raw;
+      if (rep_on) y = y > 0.0f ? __fdiv_rn(y, p.repetition_penalty) : __fmul_rn(y, p.repetition_penalty);
+      if (pf_on) y = __fsub_rn(y, __fadd_rn(__fmul_rn(p.frequency_penalty, static_cast<float>(c)), p.presence_penalty));
+      if (raw == neg_inf()) y = neg_inf();
+      hval[s] = __float_as_int(y);
+      const uint32_t hb = (static_cast<uint32_t>(id) * 0x85EBCA77u) >> 20;
+      atomicOr(&bloom[hb >> 5], 1u << (hb & 31));
+      if (!(raw >= th) && y >= th) {
+        const int pos = atomicAdd(&sm.cand_count, 1);
+        if (pos < kCandMax) { cand_y[pos] = y; cand_id[pos] = id; }
+      }
+    }
+    hist.active = 1;
+    __syncthreads();
+  };
+
+  const bool greedy = !(p.temperature > 0.0f);
+  const bool topk = p.top_k > 0 && p.top_k < V;
+  const bool fast = greedy || (topk && p.top_k <= kFastMaxK) || V <= kCandMax;
+  int out_id = -1;
+  float out_prob = 0.0f;
+  bool done = false;
+
+  if (fast) {
+    const int keff = greedy ? 1 : (topk ? p.top_k : V);
+    const unsigned int need = static_cast<unsigned int>(keff < V ? keff : 1);
+    const float tgt = 2.0f * static_cast<float>(keff) + 128.0f;
+
+    // Append every vector element >= th from vector index j0 on (and the
+    // head / tail scalars when with_scalars) -- the streaming pass.
+    auto collect = [&](float th, int j0, bool with_scalars) {
+      if (with_scalars) {
+        int sc_id = -1;
+        if (t < head) sc_id = t;
+        else if (t - head < V - tail0) sc_id = tail0 + (t - head);
+        float sc = neg_inf();
+        if (sc_id >= 0) {
+          sc = E::load(row, sc_id);
+          if (mask && !mask_allows(mask, sc_id)) sc = neg_inf();
+        }
+        warp_append<1, kCandMax>((sc_id >= 0 && sc >= th) ? 1u : 0u, &sc, sc_id, cand_y, cand_id,
+                                 &sm.cand_count);
+      }
+      for (int jb = j0; jb < nvec; jb += kUnroll * kSampleNT) {
+        uint4 w[kUnroll];
+#pragma unroll
+        for (int q = 0; q < kUnroll; q++) {
+          const int j = jb + q * kSampleNT + t;
+          if (j < nvec) w[q] = ldg_stream(vrow + j);
+        }
+#pragma unroll
+        for (int q = 0; q < kUnroll; q++) {
+          if (jb + q * kSampleNT >= nvec) break;  // warp-uniform
+          const int j = jb + q * kSampleNT + t;
+          const bool ok = j < nvec;
+          float x[EPV];
+          E::unpack(w[q], x);
+          float vm = neg_inf();
+          if (ok) {
+            if (mask) {
+              const uint32_t bits = mask_bits(mask, head + j * EPV, EPV);
+#pragma unroll
+              for (int e = 0; e < EPV; e++)
+                if (!((bits >> e) & 1u)) x[e] = neg_inf();
+            }
+#pragma unroll
+            for (int e = 0; e < EPV; e++) vm = fmaxf(vm, x[e]);
+          }
+          if (ok && vm >= th) {  // rare: only the lanes holding a hit append
+            uint32_t hits = 0;
+#pragma unroll
+            for (int e = 0; e < EPV; e++) hits |= (x[e] >= th ? 1u : 0u) << e;
+            int pos = atomicAdd(&sm.cand_count, __popc(hits));
+#pragma unroll
+            for (int e = 0; e < EPV; e++) {
+              if ((hits >> e) & 1u) {
+                if (pos < kCandMax) { cand_y[pos] = x[e]; cand_id[pos] = head + j * EPV + e; }
+                pos++;
+              }
+            }
+          }
+        }
+      }
+    };
+
+    // Sample: the first SV vectors of every thread; their per-vector maxima
+    // give the threshold for the rest of the row.
+    auto sample_vmax = [&](uint4* raw, float* vm) {
+#pragma unroll
+      for (int q = 0; q < SV; q++) {
+        const int j = t + q * kSampleNT;
+        vm[q] = neg_inf();
+        if (j < nvec) {
+          raw[q] = ldg_stream(vrow + j);
+          float x[EPV];
+          E::unpack(raw[q], x);
+          const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
+#pragma unroll
+          for (int e = 0; e < EPV; e++)
+            if ((bits >> e) & 1u) vm[q] = fmaxf(vm[q], x[e]);
+        }
+      }
+    };
+    const int nsv = nvec < SV * kSampleNT ? nvec : SV * kSampleNT;
+    const int sampled = nsv * EPV;
+    auto rank_for = [&](float mult) {
+      int rr = static_cast<int>(ceilf(mult * tgt * static_cast<float>(sampled > 0 ? sampled : 1) /
+                                      static_cast<float>(V)));
+      return static_cast<unsigned int>(rr < 1 ? 1 : rr);
+    };
+
+    float theta = neg_inf();
+    unsigned int rk = 0;
+    {
+      uint4 raw[SV];
+      float vm[SV];
+      sample_vmax(raw, vm);
+      if (V > kCandMax && sampled > 0) {
+        rk = rank_for(1.0f);
+        theta = rk > static_cast<unsigned int>(nsv) ? neg_inf() : sample_threshold<SV>(vm, rk, sm);
+      }
+      if (t == 0) sm.cand_count = 0;
+      __syncthreads();
+#pragma unroll
+      for (int q = 0; q < SV; q++) {
+        const int j = t + q * kSampleNT;
+        uint32_t hits = 0;
+        float x[EPV];
+        E::unpack(raw[q], x);
+        if (j < nvec) {
+          const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
+#pragma unroll
+          for (int e = 0; e < EPV; e++) {
+            if (!((bits >> e) & 1u)) x[e] = neg_inf();
+            hits |= (x[e] >= theta ? 1u : 0u) << e;
+          }
+        }
+        warp_append<EPV, kCandMax>(hits, x, head + j * EPV, cand_y, cand_id, &sm.cand_count);
+      }
+    }
+    collect(theta, SV * kSampleNT, true);
+    __syncthreads();
+
+    for (int attempt = 0;; attempt++) {
+      if (need_hist) {
+        const int n0 = sm.cand_count < kCandMax ? sm.cand_count : kCandMax;
+        if (!hist.active) {
+          build_hist(theta);  // appends after n0: those already hold penalised values
+        } else {  // retry: the hash exists; append the risers for the new theta
+          for (int s = t; s < ht; s += kSampleNT) {
+            const int id = hkey[s];
+            if (id < 0) continue;
+            float raw = E::load(row, id);
+            if (mask && !mask_allows(mask, id)) raw = neg_inf();
+            const float py = __int_as_float(hval[s]);
+            if (!(raw >= theta) && py >= theta) {
+              const int pos = atomicAdd(&sm.cand_count, 1);
+              if (pos < kCandMax) { cand_y[pos] = py; cand_id[pos] = id; }
+            }
+          }
+          __syncthreads();
+        }
+        for (int i = t; i < n0; i += kSampleNT) {  // raw -> penalised for history ids
+          float py;
+          if (hist.find(cand_id[i], py)) cand_y[i] = py;
+        }
+        __syncthreads();
+      }
+      const int cnt = sm.cand_count;
+      const bool overflow = cnt > kCandMax;
+      SmemSrc src{cand_y, cand_id, overflow ? kCandMax : cnt, theta};
+      const unsigned int nvalid = block_count_if(src, theta, sm);
+      if (t == 0) atomicAdd(&a.counters[5], static_cast<unsigned long long>(cnt));
+      if (!overflow && nvalid >= need) {
+        done = finish_cands(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob);
+        if (done) {
+          if (t == 0) atomicAdd(&a.counters[0], 1ull);
+          break;
+        }
+        if (t == 0) atomicAdd(&a.counters[3], 1ull);
+      } else if (t == 0) {
+        atomicAdd(&a.counters[overflow ? 1 : 2], 1ull);
+      }
+      if (attempt == kRetries || theta == neg_inf()) break;
+      // retry from L2 with a new threshold
+      float nt;
+      if (overflow) {  // the tgt-th largest buffered value bounds the k-th from below
+        uint32_t tk; unsigned long long b0, m0; unsigned int c0, n0;
+        const unsigned int tr = static_cast<unsigned int>(tgt);
+        radix_find<kSampleNT, true, false>(
+            src, 32,
+            [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; },
+            [&](unsigned long long, unsigned int c) { return c >= tr; }, sm, tk, b0, c0, n0, m0, 16);
+        nt = key2f(tk);
+        if (!(nt > theta)) nt = neg_inf();
+      } else {  // too few: a 4x deeper rank in the sample
+        rk = rk * 4u;
+        uint4 raw[SV];
+        float vm[SV];
+        sample_vmax(raw, vm);
+        nt = rk > static_cast<unsigned int>(nsv) ? neg_inf() : sample_threshold<SV>(vm, rk, sm);
+        if (!(nt < theta)) nt = neg_inf();
+      }
+      theta = nt;
+      if (V > kCandMax && theta == neg_inf()) break;  // nothing left but the full row
+      if (t == 0) sm.cand_count = 0;
+      __syncthreads();
+      collect(theta, 0, true);
+      __syncthreads();
+    }
+  }
+  if (!done) {
+    if (t == 0) atomicAdd(&a.counters[4], 1ull);
+    build_hist(__int_as_float(0x7f800000));
+    GlobalSrc<DT> src{row, V, head, nvec, tail0, mask, hist};
+    finish_row(src, p, V, u, false, neg_inf(), sm, out_id, out_prob);
+  }
+  if (t == 0) {
+    a.out_ids[b] = out_id;
+    if (a.out_probs) a.out_probs[b] = out_prob;
+  }
+}
+
+}  // namespace tg

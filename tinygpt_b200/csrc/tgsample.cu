@@ -1,0 +1,313 @@
+// tgsample.cu -- C ABI of the sampling engine (include/tgsample.h).
+//
+// Host side: argument checks, launch configuration and the host-buffer
+// variants.  No allocation happens in tg_sample / tg_spec_verify except the
+// first growth of the verification statistics buffer.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/tgsample.h"
+#include "tg_sample.cuh"
+#include "tg_spec.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int32_t cuda_fail(cudaError_t e, const char* what) {
+  return fail(TG_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define TG_CUDA(call)                                 \
+  do {                                                \
+    cudaError_t e_ = (call);                          \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+  } while (0)
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev_);
+    if (prev_ != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != prev_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = 0;
+};
+
+// Device buffer that only grows.
+struct DevBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  cudaError_t ensure(size_t n) {
+    if (n <= cap) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+    cudaError_t e = cudaMalloc(&p, n);
+    if (e == cudaSuccess) cap = n;
+    return e;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+};
+
+}  // namespace
+
+struct tg_sampler {
+  int device = 0;
+  int vocab = 0;
+  int max_batch = 0;
+  uint32_t* d_status = nullptr;  // device error word
+  unsigned long long* d_counters = nullptr;  // TG_PATH_* counters
+  DevBuf stats;                  // spec-verify statistics
+  // staging for tg_sample_host
+  DevBuf h_logits, h_params, h_hist, h_hlen, h_mask, h_state, h_unif, h_out, h_prob;
+  cudaStream_t stream = nullptr;  // used by tg_sample_host only
+  std::mutex mu;
+};
+
+extern "C" {
+
+int32_t tg_abi_version(void) { return (1 << 16) | 0; }
+
+const char* tg_last_error_string(void) { return g_last_error.c_str(); }
+
+int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_sampler** out) {
+  if (!out) return fail(TG_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  if (vocab <= 0 || vocab > TG_MAX_VOCAB) return fail(TG_ERR_UNSUPPORTED, "vocab outside [1, TG_MAX_VOCAB]");
+  if (max_batch <= 0) return fail(TG_ERR_INVALID_ARG, "max_batch must be positive");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+    return fail(TG_ERR_NO_DEVICE, "CUDA device not present");
+  DeviceGuard g(device);
+  tg_sampler* s = new tg_sampler();
+  s->device = device;
+  s->vocab = vocab;
+  s->max_batch = max_batch;
+  cudaError_t e = cudaMalloc(&s->d_status, sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(s->d_status, 0, sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&s->d_counters, sizeof(unsigned long long) * TG_PATH_COUNTERS);
+  if (e == cudaSuccess) e = cudaMemset(s->d_counters, 0, sizeof(unsigned long long) * TG_PATH_COUNTERS);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+  const int max_smem = 200 * 1024;
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tg::sample_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tg::sample_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (e != cudaSuccess) {
+    tg_sampler_destroy(s);
+    return cuda_fail(e, "tg_sampler_create");
+  }
+  *out = s;
+  return TG_OK;
+}
+
+int32_t tg_sampler_destroy(tg_sampler* s) {
+  if (!s) return TG_OK;
+  {
+    DeviceGuard g(s->device);
+    if (s->d_status) cudaFree(s->d_status);
+    if (s->d_counters) cudaFree(s->d_counters);
+    s->stats.release();
+    for (DevBuf* b : {&s->h_logits, &s->h_params, &s->h_hist, &s->h_hlen, &s->h_mask, &s->h_state,
+                      &s->h_unif, &s->h_out, &s->h_prob})
+      b->release();
+    if (s->stream) cudaStreamDestroy(s->stream);
+  }
+  delete s;
+  return TG_OK;
+}
+
+int32_t tg_sample(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_stride,
+                  int32_t batch, const tg_row_params* params, const int32_t* history,
+                  const int32_t* history_len, int32_t history_stride,
+                  const uint32_t* mask_table, int32_t num_states, const int32_t* state_id,
+                  const float* uniforms, int32_t* out_ids, float* out_probs, void* stream) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (dtype != TG_DTYPE_F32 && dtype != TG_DTYPE_BF16) return fail(TG_ERR_INVALID_ARG, "dtype must be TG_DTYPE_F32 or TG_DTYPE_BF16");
+  if (batch < 0 || batch > s->max_batch) return fail(TG_ERR_INVALID_ARG, "batch outside [0, max_batch]");
+  if (batch == 0) return TG_OK;
+  if (!logits || !params || !out_ids) return fail(TG_ERR_INVALID_ARG, "logits, params and out_ids are required");
+  if (row_stride < s->vocab) return fail(TG_ERR_INVALID_ARG, "row_stride < vocab");
+  const bool has_hist = history_len != nullptr;
+  if (has_hist && (!history || history_stride <= 0)) return fail(TG_ERR_INVALID_ARG, "history_len given without history / history_stride");
+  const bool has_mask = state_id != nullptr;
+  if (has_mask && (!mask_table || num_states <= 0)) return fail(TG_ERR_INVALID_ARG, "state_id given without mask_table / num_states");
+
+  tg::SampleArgs a{};
+  a.logits = logits;
+  a.row_stride = row_stride;
+  a.vocab = s->vocab;
+  a.batch = batch;
+  a.params = params;
+  a.history = has_hist ? history : nullptr;
+  a.history_len = has_hist ? history_len : nullptr;
+  a.history_stride = has_hist ? history_stride : 0;
+  a.hist_cap = has_hist ? (history_stride < TG_MAX_HISTORY ? history_stride : TG_MAX_HISTORY) : 0;
+  a.ht_log2 = 0;
+  if (a.hist_cap > 0) {
+    int l = 5;
+    while ((1 << l) < 2 * a.hist_cap) l++;
+    a.ht_log2 = l;
+  }
+  a.mask_table = has_mask ? mask_table : nullptr;
+  a.num_states = has_mask ? num_states : 0;
+  a.mask_words = (s->vocab + 31) / 32;
+  a.state_id = has_mask ? state_id : nullptr;
+  a.uniforms = uniforms;
+  a.out_ids = out_ids;
+  a.out_probs = out_probs;
+  a.status = s->d_status;
+  a.counters = s->d_counters;
+  const size_t smem = static_cast<size_t>(tg::kCandMax) * 12 + (a.ht_log2 ? (size_t(8) << a.ht_log2) : 0);
+  DeviceGuard g(s->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TG_DTYPE_F32)
+    tg::sample_kernel<0><<<batch, tg::kSampleNT, smem, st>>>(a);
+  else
+    tg::sample_kernel<1><<<batch, tg::kSampleNT, smem, st>>>(a);
+  TG_CUDA(cudaGetLastError());
+  return TG_OK;
+}
+
+int32_t tg_sample_host(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_stride,
+                       int32_t batch, const tg_row_params* params, const int32_t* history,
+                       const int32_t* history_len, int32_t history_stride,
+                       const uint32_t* mask_table, int32_t num_states, const int32_t* state_id,
+                       const float* uniforms, int32_t* out_ids, float* out_probs) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (batch <= 0) return batch == 0 ? TG_OK : fail(TG_ERR_INVALID_ARG, "batch < 0");
+  if (!logits || !params || !out_ids) return fail(TG_ERR_INVALID_ARG, "logits, params and out_ids are required");
+  if (dtype != TG_DTYPE_F32 && dtype != TG_DTYPE_BF16) return fail(TG_ERR_INVALID_ARG, "bad dtype");
+  if (batch > s->max_batch) return fail(TG_ERR_INVALID_ARG, "batch > max_batch");
+  if (row_stride < s->vocab) return fail(TG_ERR_INVALID_ARG, "row_stride < vocab");
+  std::lock_guard<std::mutex> lk(s->mu);
+  DeviceGuard g(s->device);
+  cudaStream_t st = s->stream;
+  const size_t esz = dtype == TG_DTYPE_F32 ? 4 : 2;
+  const size_t nlog = static_cast<size_t>(batch) * row_stride * esz;
+  TG_CUDA(s->h_logits.ensure(nlog));
+  TG_CUDA(s->h_params.ensure(sizeof(tg_row_params) * batch));
+  TG_CUDA(s->h_out.ensure(sizeof(int32_t) * batch));
+  TG_CUDA(cudaMemcpyAsync(s->h_logits.p, logits, nlog, cudaMemcpyHostToDevice, st));
+  TG_CUDA(cudaMemcpyAsync(s->h_params.p, params, sizeof(tg_row_params) * batch, cudaMemcpyHostToDevice, st));
+  const int32_t* d_hist = nullptr;
+  const int32_t* d_hlen = nullptr;
+  if (history_len) {
+    if (!history || history_stride <= 0) return fail(TG_ERR_INVALID_ARG, "history_len given without history");
+    const size_t nh = sizeof(int32_t) * static_cast<size_t>(batch) * history_stride;
+    TG_CUDA(s->h_hist.ensure(nh));
+    TG_CUDA(s->h_hlen.ensure(sizeof(int32_t) * batch));
+    TG_CUDA(cudaMemcpyAsync(s->h_hist.p, history, nh, cudaMemcpyHostToDevice, st));
+    TG_CUDA(cudaMemcpyAsync(s->h_hlen.p, history_len, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
+    d_hist = static_cast<const int32_t*>(s->h_hist.p);
+    d_hlen = static_cast<const int32_t*>(s->h_hlen.p);
+  }
+  const uint32_t* d_mask = nullptr;
+  const int32_t* d_state = nullptr;
+  if (state_id) {
+    if (!mask_table || num_states <= 0) return fail(TG_ERR_INVALID_ARG, "state_id given without mask_table");
+    const size_t nm = sizeof(uint32_t) * static_cast<size_t>(num_states) * ((s->vocab + 31) / 32);
+    TG_CUDA(s->h_mask.ensure(nm));
+    TG_CUDA(s->h_state.ensure(sizeof(int32_t) * batch));
+    TG_CUDA(cudaMemcpyAsync(s->h_mask.p, mask_table, nm, cudaMemcpyHostToDevice, st));
+    TG_CUDA(cudaMemcpyAsync(s->h_state.p, state_id, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
+    d_mask = static_cast<const uint32_t*>(s->h_mask.p);
+    d_state = static_cast<const int32_t*>(s->h_state.p);
+  }
+  const float* d_unif = nullptr;
+  if (uniforms) {
+    TG_CUDA(s->h_unif.ensure(sizeof(float) * batch));
+    TG_CUDA(cudaMemcpyAsync(s->h_unif.p, uniforms, sizeof(float) * batch, cudaMemcpyHostToDevice, st));
+    d_unif = static_cast<const float*>(s->h_unif.p);
+  }
+  float* d_prob = nullptr;
+  if (out_probs) {
+    TG_CUDA(s->h_prob.ensure(sizeof(float) * batch));
+    d_prob = static_cast<float*>(s->h_prob.p);
+  }
+  int32_t rc = tg_sample(s, s->h_logits.p, dtype, row_stride, batch,
+                         static_cast<const tg_row_params*>(s->h_params.p), d_hist, d_hlen,
+                         history_stride, d_mask, num_states, d_state, d_unif,
+                         static_cast<int32_t*>(s->h_out.p), d_prob, st);
+  if (rc != TG_OK) return rc;
+  TG_CUDA(cudaMemcpyAsync(out_ids, s->h_out.p, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, st));
+  if (out_probs)
+    TG_CUDA(cudaMemcpyAsync(out_probs, d_prob, sizeof(float) * batch, cudaMemcpyDeviceToHost, st));
+  TG_CUDA(cudaStreamSynchronize(st));
+  return TG_OK;
+}
+
+int32_t tg_spec_verify(tg_sampler* s, const void* target_logits, const void* draft_logits,
+                       int32_t dtype, int32_t batch, int32_t K, const int32_t* draft_ids,
+                       const float* temperature, const float* u_accept, const float* u_draw,
+                       int32_t* out_ids, int32_t* out_n, void* stream) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (dtype != TG_DTYPE_F32 && dtype != TG_DTYPE_BF16) return fail(TG_ERR_INVALID_ARG, "bad dtype");
+  if (batch < 0 || batch > s->max_batch) return fail(TG_ERR_INVALID_ARG, "batch outside [0, max_batch]");
+  if (K < 0 || K > 64) return fail(TG_ERR_UNSUPPORTED, "K outside [0, 64]");
+  if (batch == 0) return TG_OK;
+  if (!target_logits || !temperature || !out_ids || !out_n || (K > 0 && !draft_ids))
+    return fail(TG_ERR_INVALID_ARG, "target_logits, draft_ids, temperature, out_ids and out_n are required");
+  if (K > 0 && (!draft_logits || !u_accept)) return fail(TG_ERR_INVALID_ARG, "draft_logits and u_accept are required when K > 0");
+  if (!u_draw) return fail(TG_ERR_INVALID_ARG, "u_draw is required");
+  std::lock_guard<std::mutex> lk(s->mu);
+  DeviceGuard g(s->device);
+  const size_t nst = sizeof(tg::SpecStat) * static_cast<size_t>(batch) * (2 * K + 1);
+  TG_CUDA(s->stats.ensure(nst));
+  tg::SpecArgs a{target_logits, draft_logits, batch, K, s->vocab, draft_ids, temperature,
+                 u_accept, u_draw, out_ids, out_n, static_cast<tg::SpecStat*>(s->stats.p),
+                 s->d_status};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nrows = batch * (2 * K + 1);
+  if (dtype == TG_DTYPE_F32) {
+    tg::spec_stats_kernel<0><<<nrows, tg::kSpecNT, 0, st>>>(a);
+    tg::spec_verify_kernel<0><<<batch, tg::kSpecNT, 0, st>>>(a);
+  } else {
+    tg::spec_stats_kernel<1><<<nrows, tg::kSpecNT, 0, st>>>(a);
+    tg::spec_verify_kernel<1><<<batch, tg::kSpecNT, 0, st>>>(a);
+  }
+  TG_CUDA(cudaGetLastError());
+  return TG_OK;
+}
+
+int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits) {
+  if (!s || !out_bits) return fail(TG_ERR_INVALID_ARG, "NULL argument");
+  DeviceGuard g(s->device);
+  TG_CUDA(cudaDeviceSynchronize());
+  TG_CUDA(cudaMemcpy(out_bits, s->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  TG_CUDA(cudaMemset(s->d_status, 0, sizeof(uint32_t)));
+  return TG_OK;
+}
+
+int32_t tg_sampler_path_counters(tg_sampler* s, uint64_t* out, int32_t n, int32_t reset) {
+  if (!s || !out || n <= 0) return fail(TG_ERR_INVALID_ARG, "NULL argument or n <= 0");
+  DeviceGuard g(s->device);
+  TG_CUDA(cudaDeviceSynchronize());
+  unsigned long long tmp[TG_PATH_COUNTERS];
+  TG_CUDA(cudaMemcpy(tmp, s->d_counters, sizeof(tmp), cudaMemcpyDeviceToHost));
+  for (int i = 0; i < n && i < TG_PATH_COUNTERS; i++) out[i] = tmp[i];
+  if (reset) TG_CUDA(cudaMemset(s->d_counters, 0, sizeof(tmp)));
+  return TG_OK;
+}
+
+}  // extern "C"
