@@ -154,6 +154,28 @@ int32_t tg_spec_verify(tg_sampler* s, const void* target_logits,
                        const float* u_draw, int32_t* out_ids, int32_t* out_n,
                        void* stream);
 
+/* Allocation-free variant of tg_spec_verify.  No counterpart in the reference.
+ * For callers that cannot call cudaMalloc: for example a serving process that
+ * reserved all free HBM for its KV cache at start-up (a cudaMalloc would fail),
+ * or a decode loop that must not pay the device-wide synchronization cudaMalloc
+ * and cudaFree may cause.  It takes no handle and allocates nothing: the
+ * per-position statistics live in a fixed array inside the library, sized for
+ * batch * (2K + 1) <= TG_STATIC_SPEC_MAX_ROWS vocab rows (larger calls return
+ * TG_ERR_UNSUPPORTED).  Every GPU that loads the library holds that array
+ * (about 128 KiB) until the process exits.  The first call on a device looks up
+ * the array's device address with that device current; make that first call
+ * before any stream capture.  All calls on a device share the array, so calls
+ * that overlap on the GPU (different streams without ordering) race.
+ * Arguments and results are those of tg_spec_verify, on CUDA device `device`;
+ * an out-of-range draft id counts as a rejection and is not reported. */
+#define TG_STATIC_SPEC_MAX_ROWS 8192
+int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_logits,
+                              const void* draft_logits, int32_t dtype, int32_t batch,
+                              int32_t K, const int32_t* draft_ids,
+                              const float* temperature, const float* u_accept,
+                              const float* u_draw, int32_t* out_ids, int32_t* out_n,
+                              void* stream);
+
 /* Device error word of the last completed call on this handle (synchronizes
  * the handle's device).  Bit 0: a state_id outside [0, num_states);
  * bit 1: a draft id outside [0, vocab).  Cleared by this call. */

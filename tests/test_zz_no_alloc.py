@@ -1,0 +1,54 @@
+"""The allocation-free speculative verification entry point (tg_spec_verify_static).
+
+Some callers of this library cannot call cudaMalloc: a serving process that has
+reserved all free HBM for its KV cache, or a decode loop that must not take the
+device-wide synchronization an allocation can cause.  tg_spec_verify_static
+keeps its scratch in a fixed array inside the library instead.  This test calls
+it through the C ABI twice in a row (the array keeps the previous call's
+contents) and checks both results against tg_spec_verify, bit for bit -- the
+tolerance every parity test here uses.  The file is named to be collected last.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from tinygpt_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+
+def test_static_scratch_entry_matches_allocating_entry(cuda_lib):
+    import torch
+    from tinygpt_b200 import _lib
+    from tinygpt_b200.sampler import Sampler
+
+    V = 5003
+    s = Sampler(V, 64, 0)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    for seed, B in ((21, 24), (22, 40)):  # two calls in a row, different shapes
+        w = W.make(5, seed=seed, batch=B, vocab=V)
+        w["temperature"][::4] = 0.0  # some greedy rows too
+        dev = {k: torch.from_numpy(np.ascontiguousarray(w[k])).cuda()
+               for k in ("target", "draft", "draft_ids", "temperature", "u_accept", "u_draw")}
+        K = w["draft_ids"].shape[1]
+        ref_ids, ref_n = s.spec_verify(dev["target"], dev["draft"], dev["draft_ids"],
+                                       dev["temperature"], dev["u_accept"], dev["u_draw"])
+        ids = torch.full((B, K + 1), -7, dtype=torch.int32, device="cuda:0")
+        n = torch.full((B,), -7, dtype=torch.int32, device="cuda:0")
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rc = cuda_lib.tg_spec_verify_static(0, V, P(dev["target"]), P(dev["draft"]),
+                                            _lib.TG_DTYPE_F32, B, K, P(dev["draft_ids"]),
+                                            P(dev["temperature"]), P(dev["u_accept"]),
+                                            P(dev["u_draw"]), P(ids), P(n), stream)
+        assert rc == _lib.TG_OK, cuda_lib.tg_last_error_string()
+        torch.cuda.synchronize()
+        assert torch.equal(n, ref_n)
+        assert torch.equal(ids, ref_ids)
+    # beyond the static scratch: rejected with a clear error, nothing launched
+    rc = cuda_lib.tg_spec_verify_static(0, V, P(dev["target"]), P(dev["draft"]),
+                                        _lib.TG_DTYPE_F32, _lib.TG_STATIC_SPEC_MAX_ROWS, K,
+                                        P(dev["draft_ids"]), P(dev["temperature"]),
+                                        P(dev["u_accept"]), P(dev["u_draw"]), P(ids), P(n), stream)
+    assert rc == _lib.TG_ERR_UNSUPPORTED
+    assert b"TG_STATIC_SPEC_MAX_ROWS" in cuda_lib.tg_last_error_string()

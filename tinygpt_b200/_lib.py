@@ -23,6 +23,7 @@ TG_DTYPE_F32 = 0
 TG_DTYPE_BF16 = 1
 TG_MAX_VOCAB = 1 << 20
 TG_MAX_HISTORY = 4096
+TG_STATIC_SPEC_MAX_ROWS = 8192
 
 ROW_PARAMS_DTYPE = np.dtype([
     ("temperature", np.float32), ("top_p", np.float32), ("min_p", np.float32),
@@ -31,7 +32,8 @@ ROW_PARAMS_DTYPE = np.dtype([
 ])
 
 EXPORTED = ["tg_abi_version", "tg_last_error_string", "tg_sampler_create", "tg_sampler_destroy",
-            "tg_sample", "tg_sample_host", "tg_spec_verify", "tg_sampler_device_status", "tg_sampler_path_counters"]
+            "tg_sample", "tg_sample_host", "tg_spec_verify", "tg_sampler_device_status", "tg_sampler_path_counters",
+            "tg_spec_verify_static"]
 
 
 class TGError(RuntimeError):
@@ -71,6 +73,8 @@ def load(path: str = LIB_PATH):
     L.tg_sampler_device_status.restype = i32
     L.tg_sampler_path_counters.argtypes = [vp, vp, i32, i32]
     L.tg_sampler_path_counters.restype = i32
+    L.tg_spec_verify_static.argtypes = [i32, i32, vp, vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]
+    L.tg_spec_verify_static.restype = i32
     _LIB = L
     return L
 

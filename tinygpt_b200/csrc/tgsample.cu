@@ -69,6 +69,30 @@ struct DevBuf {
   }
 };
 
+// Scratch of tg_spec_verify_static: TG_STATIC_SPEC_MAX_ROWS statistics records
+// followed by one status word.  In host code this name is only a stand-in for
+// the device array; its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_static_spec_scratch[
+    TG_STATIC_SPEC_MAX_ROWS * sizeof(tg::SpecStat) + 256];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices] = {};
+
+// Device address of the static scratch on the current device `dev` (looked up
+// once per device, with that device current).
+cudaError_t static_scratch(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_spec_scratch);
+    if (e != cudaSuccess) return e;
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return cudaSuccess;
+}
+
 }  // namespace
 
 struct tg_sampler {
@@ -278,6 +302,44 @@ int32_t tg_spec_verify(tg_sampler* s, const void* target_logits, const void* dra
                  u_accept, u_draw, out_ids, out_n, static_cast<tg::SpecStat*>(s->stats.p),
                  s->d_status};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nrows = batch * (2 * K + 1);
+  if (dtype == TG_DTYPE_F32) {
+    tg::spec_stats_kernel<0><<<nrows, tg::kSpecNT, 0, st>>>(a);
+    tg::spec_verify_kernel<0><<<batch, tg::kSpecNT, 0, st>>>(a);
+  } else {
+    tg::spec_stats_kernel<1><<<nrows, tg::kSpecNT, 0, st>>>(a);
+    tg::spec_verify_kernel<1><<<batch, tg::kSpecNT, 0, st>>>(a);
+  }
+  TG_CUDA(cudaGetLastError());
+  return TG_OK;
+}
+
+int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_logits,
+                              const void* draft_logits, int32_t dtype, int32_t batch, int32_t K,
+                              const int32_t* draft_ids, const float* temperature,
+                              const float* u_accept, const float* u_draw, int32_t* out_ids,
+                              int32_t* out_n, void* stream) {
+  if (dtype != TG_DTYPE_F32 && dtype != TG_DTYPE_BF16) return fail(TG_ERR_INVALID_ARG, "bad dtype");
+  if (vocab <= 0 || vocab > TG_MAX_VOCAB) return fail(TG_ERR_UNSUPPORTED, "vocab outside [1, TG_MAX_VOCAB]");
+  if (batch < 0 || K < 0 || K > 64) return fail(TG_ERR_INVALID_ARG, "batch < 0 or K outside [0, 64]");
+  if (static_cast<int64_t>(batch) * (2 * K + 1) > TG_STATIC_SPEC_MAX_ROWS)
+    return fail(TG_ERR_UNSUPPORTED, "batch * (2K + 1) exceeds TG_STATIC_SPEC_MAX_ROWS (the static scratch)");
+  if (batch == 0) return TG_OK;
+  if (!target_logits || !temperature || !out_ids || !out_n || !u_draw || (K > 0 && (!draft_ids || !draft_logits || !u_accept)))
+    return fail(TG_ERR_INVALID_ARG, "missing required pointer");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev || device >= kMaxDevices)
+    return fail(TG_ERR_NO_DEVICE, "CUDA device not present");
+  DeviceGuard g(device);
+  void* scratch = nullptr;
+  TG_CUDA(static_scratch(device, &scratch));
+  tg::SpecStat* stats = static_cast<tg::SpecStat*>(scratch);
+  uint32_t* status = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) +
+                                                 TG_STATIC_SPEC_MAX_ROWS * sizeof(tg::SpecStat));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  TG_CUDA(cudaMemsetAsync(status, 0, sizeof(uint32_t), st));
+  tg::SpecArgs a{target_logits, draft_logits, batch, K, vocab, draft_ids, temperature,
+                 u_accept, u_draw, out_ids, out_n, stats, status};
   const int nrows = batch * (2 * K + 1);
   if (dtype == TG_DTYPE_F32) {
     tg::spec_stats_kernel<0><<<nrows, tg::kSpecNT, 0, st>>>(a);
