@@ -9,9 +9,15 @@ namespace tg {
 constexpr unsigned kFull = 0xffffffffu;
 
 struct __align__(16) BlockScratch {
-  unsigned long long hmass[256];
-  unsigned int hcnt[256];
-  unsigned int hfine[256];  // elements whose key has non-zero low 16 bits (kEarly16)
+  union {
+    struct {
+      unsigned long long hmass[256];
+      unsigned int hcnt[256];
+      unsigned int hfine[256];  // elements whose key has non-zero low 16 bits (kEarly16)
+    };
+    unsigned int hc[2048];        // wide count histogram (hist_round)
+    unsigned long long hm[1024];  // wide mass histogram (hist_round)
+  };
   unsigned long long red_u64[32];
   float red_f[32];
   int red_i[32];
@@ -21,6 +27,12 @@ struct __align__(16) BlockScratch {
   unsigned int sel_cbefore;
   unsigned int sel_cnt;
   int cand_count;
+  // small list for warp-level resolution of one histogram bin
+  unsigned long long sk[32];
+  unsigned long long sw[32];
+  int sid[32];
+  int sn;
+  float red_f2[32];
 };
 
 template <int NT>
@@ -43,6 +55,18 @@ __device__ __forceinline__ unsigned long long block_sum(unsigned long long v, Bl
   unsigned long long r = 0;
 #pragma unroll
   for (int i = 0; i < NT / 32; i++) r += sm.red_u64[i];
+  __syncthreads();
+  return r;
+}
+
+template <int NT>
+__device__ __forceinline__ unsigned int block_max_u32(unsigned int v, BlockScratch& sm) {
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(kFull, v, o));
+  if ((threadIdx.x & 31) == 0) sm.red_i[threadIdx.x >> 5] = static_cast<int>(v);
+  __syncthreads();
+  unsigned int r = static_cast<unsigned int>(sm.red_i[0]);
+#pragma unroll
+  for (int i = 1; i < NT / 32; i++) r = max(r, static_cast<unsigned int>(sm.red_i[i]));
   __syncthreads();
   return r;
 }
@@ -121,6 +145,122 @@ __device__ __forceinline__ void warp_append(uint32_t hits, const float* x, int e
       pos++;
     }
   }
+}
+
+// One histogram round with NB bins (NB a multiple of NT) and an all-thread scan.
+// binw(i, y, bin, w) -> bool: whether the element takes part and its bin, given
+// in scan order (the caller maps descending keys to ascending bins).  Returns
+// the first bin at which reached(cumulative weight) holds, the weight before it
+// and the weight in it.  Weights are counts (kMass = false) or u64 masses.
+// reached(0) must be false and reached(total) true.
+struct HistSel {
+  int bin;
+  unsigned long long before;
+  unsigned long long in_bin;
+};
+
+template <int NT, int NB, bool kMass, class Src, class BinW, class Reached>
+__device__ HistSel hist_round(const Src& src, BinW binw, Reached reached, BlockScratch& sm) {
+  static_assert(NB % NT == 0, "bins must be a multiple of the block");
+  static_assert(kMass ? NB <= 1024 : NB <= 2048, "histogram does not fit");
+  constexpr int P = NB / NT;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int j = 0; j < P; j++) {
+    if (kMass) sm.hm[t * P + j] = 0ull;
+    else sm.hc[t * P + j] = 0u;
+  }
+  if (t == 0) sm.sel_bin = 0xffffffffu;
+  __syncthreads();
+  src.for_each([&](int i, float y) {
+    int bin;
+    unsigned long long w;
+    if (!binw(i, y, bin, w)) return;
+    if (kMass) atomicAdd(&sm.hm[bin], w);
+    else atomicAdd(&sm.hc[bin], 1u);
+  });
+  __syncthreads();
+  unsigned long long v[P];
+  unsigned long long loc = 0;
+#pragma unroll
+  for (int j = 0; j < P; j++) {
+    v[j] = kMass ? sm.hm[t * P + j] : static_cast<unsigned long long>(sm.hc[t * P + j]);
+    loc += v[j];
+  }
+  unsigned long long tot;
+  const unsigned long long bef = block_excl_scan<NT>(loc, tot, sm);
+  if (!reached(bef) && reached(bef + loc)) {
+    unsigned long long c = bef;
+#pragma unroll
+    for (int j = 0; j < P; j++) {
+      if (reached(c + v[j])) {
+        sm.sel_bin = t * P + j;
+        sm.sel_before = c;
+        sm.sel_mass = v[j];
+        break;
+      }
+      c += v[j];
+    }
+  }
+  __syncthreads();
+  HistSel r{static_cast<int>(sm.sel_bin), sm.sel_before, sm.sel_mass};  // bin -1: not reached
+  __syncthreads();
+  return r;
+}
+
+// Collect the elements for which member(i, y, key, w, id) holds into the small
+// list (first 32 kept); returns how many there were.
+template <int NT, class Src, class Member>
+__device__ int collect_small(const Src& src, Member member, BlockScratch& sm) {
+  if (threadIdx.x == 0) sm.sn = 0;
+  __syncthreads();
+  src.for_each([&](int i, float y) {
+    unsigned long long key, w;
+    int id;
+    if (!member(i, y, key, w, id)) return;
+    const int pos = atomicAdd(&sm.sn, 1);
+    if (pos < 32) { sm.sk[pos] = key; sm.sw[pos] = w; sm.sid[pos] = id; }
+  });
+  __syncthreads();
+  const int n = sm.sn;
+  __syncthreads();
+  return n;
+}
+
+// Warp 0: sort the small list (n <= 32) by key ascending, then the inclusive
+// running weight from `before`; the first position where reached() holds.
+// Outputs (valid in warp 0): that position's key, weight and id, and whether
+// any position reached.
+template <class Reached>
+__device__ __forceinline__ bool warp_sorted_pick(int n, unsigned long long before, Reached reached,
+                                                 const BlockScratch& sm, unsigned long long& key,
+                                                 unsigned long long& w, int& id) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long k = lane < n ? sm.sk[lane] : ~0ull;
+  unsigned long long x = lane < n ? sm.sw[lane] : 0ull;
+  int d = lane < n ? sm.sid[lane] : 0x7fffffff;
+  for (int size = 2; size <= 32; size <<= 1) {
+    for (int j = size >> 1; j > 0; j >>= 1) {
+      const unsigned long long ok = __shfl_xor_sync(kFull, k, j);
+      const unsigned long long ox = __shfl_xor_sync(kFull, x, j);
+      const int od = __shfl_xor_sync(kFull, d, j);
+      const bool up = (lane & size) == 0;
+      const bool lower = (lane & j) == 0;
+      const bool take = (lower == up) ? (ok < k) : (ok > k);
+      if (take) { k = ok; x = ox; d = od; }
+    }
+  }
+  unsigned long long incl = x;
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long v = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += v;
+  }
+  const unsigned hit = __ballot_sync(kFull, lane < n && reached(before + incl));
+  const int src = hit ? __ffs(hit) - 1 : (n > 0 ? n - 1 : 0);
+  key = __shfl_sync(kFull, k, src);
+  w = __shfl_sync(kFull, x, src);
+  id = __shfl_sync(kFull, d, src);
+  return hit != 0;
 }
 
 // Histogram update aggregated over the lanes of a warp that hit the same bin

@@ -93,6 +93,14 @@ struct Elt<1> {  // bf16
     const uint16_t h = __ldg(reinterpret_cast<const unsigned short*>(row) + i);
     return __uint_as_float(static_cast<uint32_t>(h) << 16);
   }
+  // max of the 8 values (packed bf16x2 maxima, then one fp32 max)
+  __device__ __forceinline__ static float vmax(const uint4& w) {
+    uint32_t a, b, m;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(a) : "r"(w.x), "r"(w.y));
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(b) : "r"(w.z), "r"(w.w));
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(a), "r"(b));
+    return fmaxf(bf16_lo(m), bf16_hi(m));
+  }
 };
 
 template <>
@@ -105,6 +113,10 @@ struct Elt<0> {  // fp32
   }
   __device__ __forceinline__ static float load(const void* row, int64_t i) {
     return __ldg(reinterpret_cast<const float*>(row) + i);
+  }
+  __device__ __forceinline__ static float vmax(const uint4& w) {
+    return fmaxf(fmaxf(__uint_as_float(w.x), __uint_as_float(w.y)),
+                 fmaxf(__uint_as_float(w.z), __uint_as_float(w.w)));
   }
 };
 

@@ -39,6 +39,26 @@ constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold 
 constexpr int kUnroll = TG_UNROLL;  // 128-bit loads in flight per thread
 constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) before the full row
 constexpr int kMinCtasPerSm = 4; // occupancy target (caps registers at 64)
+constexpr int kHitCap = kCandMax / (kSampleNT / 32);  // hit vectors listed per warp
+
+// Diagnostic build only (-DTG_PHASE_TIMING): cycles per phase summed over CTAs.
+#ifdef TG_PHASE_TIMING
+__device__ unsigned long long g_phase_cycles[16];
+#endif
+struct PhaseClock {
+  long long last = 0;
+  __device__ __forceinline__ void mark(int i) {
+#ifdef TG_PHASE_TIMING
+    if (threadIdx.x == 0) {
+      const long long now = clock64();
+      if (last) atomicAdd(&g_phase_cycles[i], static_cast<unsigned long long>(now - last));
+      last = now;
+    }
+#else
+    (void)i;
+#endif
+  }
+};
 
 struct SampleArgs {
   const void* logits;
@@ -133,7 +153,8 @@ struct SmemSrc {
   __device__ __forceinline__ void for_each(F&& f) const {
     for (int i = threadIdx.x; i < n; i += kSampleNT) {
       const float v = y[i];
-      if (v >= theta) f(id[i], v);
+      const int d = id[i];
+      if (d >= 0 && v >= theta) f(d, v);
     }
   }
 };
@@ -323,38 +344,96 @@ __device__ __forceinline__ unsigned long long mass_of_e(float e) {
   return __float2ull_rz(__fmul_rn(e, kMassScale));
 }
 
-// Stages (b)-(e) over the shared-memory candidate list (all elements >= theta
-// of the row).  Same results as finish_row; returns false when an element
-// below theta could survive top-k (the caller retries with a lower theta).
+// Stages (b)-(e) over the shared-memory candidate list (every element >= theta
+// of the row).  Each selection is one wide histogram round over a monotone bin
+// function; the crossing bin is then resolved exactly by one warp (<= 32
+// members, the common case) or by the radix version above.  Returns false when
+// an element below theta could survive top-k (the caller lowers theta).
 __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
                              const tg_row_params& p, int V, float u, BlockScratch& sm,
-                             int& out_id, float& out_prob) {
+                             int& out_id, float& out_prob, PhaseClock& pc) {
   SmemSrc src{cy, cid, n, theta};
   if (!(p.temperature > 0.0f)) return finish_row(src, p, V, u, false, theta, sm, out_id, out_prob);
   const float T = p.temperature;
   const bool topk = p.top_k > 0 && p.top_k < V;
+  const int lane = threadIdx.x & 31;
+
+  float ymax = neg_inf(), nymin = neg_inf();
+  src.for_each([&](int, float y) {
+    ymax = fmaxf(ymax, y);
+    if (y > neg_inf()) nymin = fmaxf(nymin, -y);
+  });
+  ymax = block_max<kSampleNT>(ymax, sm);
+  const float ymin = -block_max<kSampleNT>(nymin, sm);
+  if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
+
   float sk = neg_inf();
   if (topk) {
-    uint32_t kkey; unsigned long long b0, m0; unsigned int c0, n0;
     const unsigned int k = static_cast<unsigned int>(p.top_k);
-    auto kw = [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; };
-    auto rc = [&](unsigned long long, unsigned int c) { return c >= k; };
-    radix_find<kSampleNT, true, false, SmemSrc, decltype(kw), decltype(rc), true>(
-        src, 32, kw, rc, sm, kkey, b0, c0, n0, m0);
+    const float width = __fsub_rn(ymax, ymin);
+    const float scale = width > 0.0f ? __fdiv_rn(2046.0f, width) : 0.0f;
+    auto binf = [&](float y) {  // descending y -> ascending bin; -inf last
+      if (!(y > neg_inf())) return 2047;
+      const int bn = static_cast<int>(__fmul_rn(__fsub_rn(ymax, y), scale));
+      return bn > 2046 ? 2046 : bn;
+    };
+    const HistSel hs = hist_round<kSampleNT, 2048, false>(
+        src, [&](int, float y, int& bin, unsigned long long& w) { bin = binf(y); w = 1; return true; },
+        [&](unsigned long long c) { return c >= k; }, sm);
+    if (hs.bin < 0) return false;
+    const unsigned int j = k - static_cast<unsigned int>(hs.before);  // rank inside the bin
+    const int nb = collect_small<kSampleNT>(
+        src,
+        [&](int i, float y, unsigned long long& key, unsigned long long& w, int& id) {
+          if (binf(y) != hs.bin) return false;
+          key = (static_cast<unsigned long long>(~fkey(y)) << 32) | static_cast<uint32_t>(i);
+          w = 1;
+          id = i;
+          return true;
+        },
+        sm);
+    uint32_t kkey;
+    if (nb <= 32) {
+      if (threadIdx.x < 32) {
+        unsigned long long key, w;
+        int id;
+        warp_sorted_pick(nb, 0ull, [&](unsigned long long c) { return c >= j; }, sm, key, w, id);
+        if (lane == 0) sm.sel_cnt = ~static_cast<uint32_t>(key >> 32);
+      }
+      __syncthreads();
+      kkey = sm.sel_cnt;
+      __syncthreads();
+    } else {
+      unsigned int lo = 0u, hi = 0u;  // max of ~key and of key over the bin
+      src.for_each([&](int, float y) {
+        if (binf(y) == hs.bin) { lo = max(lo, ~fkey(y)); hi = max(hi, fkey(y)); }
+      });
+      lo = ~block_max_u32<kSampleNT>(lo, sm);
+      hi = block_max_u32<kSampleNT>(hi, sm);
+      if (lo == hi) {
+        kkey = hi;
+      } else {
+        unsigned long long b0, m0; unsigned int c0, n0;
+        auto kw = [&](int, float y, uint32_t& key, unsigned long long& w) {
+          if (binf(y) != hs.bin) return false;
+          key = fkey(y); w = 0; return true;
+        };
+        auto rc = [&](unsigned long long, unsigned int c) { return c >= j; };
+        radix_find<kSampleNT, true, false, SmemSrc, decltype(kw), decltype(rc), true>(
+            src, 32, kw, rc, sm, kkey, b0, c0, n0, m0);
+      }
+    }
     sk = __fdiv_rn(key2f(kkey), T);
     if (theta > neg_inf() && __fdiv_rn(key2f(fkey(theta) - 1u), T) >= sk) return false;
   }
-  float ymax = neg_inf();
-  src.for_each([&](int, float y) { ymax = fmaxf(ymax, y); });
-  ymax = block_max<kSampleNT>(ymax, sm);
-  if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
+  pc.mark(5);
   const float smax = __fdiv_rn(ymax, T);
 
   // compaction: s, e in place; ids of dropped slots set to -1
   unsigned long long Q = 0;
   for (int i = threadIdx.x; i < n; i += kSampleNT) {
     const float y = cy[i];
-    bool keep = y >= theta && y > neg_inf();
+    bool keep = cid[i] >= 0 && y >= theta && y > neg_inf();
     float sv = 0.0f, e = 0.0f;
     if (keep) {
       sv = __fdiv_rn(y, T);
@@ -370,24 +449,70 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       cid[i] = -1;
     }
   }
-  Q = block_sum<kSampleNT>(Q, sm);  // (its barrier also publishes the compaction)
+  Q = block_sum<kSampleNT>(Q, sm);
   ASrc as{cy, cid, n};
+  pc.mark(6);
 
+  // (d) top-p: the last element (cut_key, cut_id) of the shortest prefix in
+  // (s desc, id asc) order whose mass reaches top_p * Q.
   const bool toppon = p.top_p < 1.0f;
   uint32_t cut_key = 0;
   int cut_id = 0x7fffffff;
   if (toppon) {
     const double tau = __dmul_rn(static_cast<double>(p.top_p), __ull2double_rn(Q));
-    unsigned long long above = 0, qt = 0;
-    unsigned int nties = 0;
-    unsigned long long jstar = 1;
-    if (!(tau > 0.0)) {
+    auto dbin = [&](float sv) {
+      const int bn = static_cast<int>(__fmul_rn(__fsub_rn(smax, sv), 32.0f));
+      return bn > 1023 ? 1023 : bn;
+    };
+    bool resolved = false;
+    if (tau > 0.0) {
+      const HistSel hs = hist_round<kSampleNT, 1024, true>(
+          as,
+          [&](int i, float sv, int& bin, unsigned long long& w) {
+            w = mass_of_e(ce[i]);
+            bin = dbin(sv);
+            return w > 0;
+          },
+          [&](unsigned long long m) { return __ull2double_rn(m) >= tau; }, sm);
+      if (hs.bin >= 0) {
+        const int nb = collect_small<kSampleNT>(
+            as,
+            [&](int i, float sv, unsigned long long& key, unsigned long long& w, int& id) {
+              w = mass_of_e(ce[i]);
+              if (w == 0 || dbin(sv) != hs.bin) return false;
+              id = cid[i];
+              key = (static_cast<unsigned long long>(~fkey(sv)) << 32) | static_cast<uint32_t>(id);
+              return true;
+            },
+            sm);
+        if (nb <= 32) {
+          if (threadIdx.x < 32) {
+            unsigned long long key, w;
+            int id;
+            warp_sorted_pick(nb, hs.before, [&](unsigned long long m) { return __ull2double_rn(m) >= tau; },
+                             sm, key, w, id);
+            if (lane == 0) { sm.sel_cnt = ~static_cast<uint32_t>(key >> 32); sm.sid[0] = id; }
+          }
+          __syncthreads();
+          cut_key = sm.sel_cnt;
+          cut_id = sm.sid[0];
+          __syncthreads();
+          resolved = true;
+        }
+      }
+    } else {  // top_p <= 0: the single top element (smallest id among the maxima)
       cut_key = fkey(smax);
-      unsigned long long c = 0;
-      as.for_each([&](int, float sv) { c += (fkey(sv) == cut_key) ? 1ull : 0ull; });
-      nties = static_cast<unsigned int>(block_sum<kSampleNT>(c, sm));
-    } else {
-      unsigned int cb;
+      unsigned int best = 0u;
+      as.for_each([&](int i, float sv) {
+        if (fkey(sv) == cut_key) best = max(best, ~static_cast<uint32_t>(cid[i]));
+      });
+      cut_id = static_cast<int>(~block_max_u32<kSampleNT>(best, sm));
+      resolved = true;
+    }
+    if (!resolved) {  // crowded bin: exact radix over the whole survivor set
+      unsigned long long above = 0, qt = 0;
+      unsigned int nties = 0, cb;
+      unsigned long long jstar = 1;
       radix_find<kSampleNT, true, true>(
           as, 32,
           [&](int i, float sv, uint32_t& key, unsigned long long& w) {
@@ -408,26 +533,26 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
         while (jstar > 1 && __ull2double_rn(above + (jstar - 1) * qt) >= tau) jstar--;
         while (jstar < nties && __ull2double_rn(above + jstar * qt) < tau) jstar++;
       }
-    }
-    if (jstar < nties) {
-      uint32_t idkey; unsigned long long b1, m1; unsigned int c1, n1;
-      const unsigned int js = static_cast<unsigned int>(jstar);
-      radix_find<kSampleNT, false, false>(
-          as, 20,
-          [&](int i, float sv, uint32_t& key, unsigned long long& w) {
-            if (fkey(sv) != cut_key) return false;
-            key = static_cast<uint32_t>(cid[i]);
-            w = 0;
-            return true;
-          },
-          [&](unsigned long long, unsigned int c) { return c >= js; }, sm, idkey, b1, c1, n1, m1);
-      cut_id = static_cast<int>(idkey);
+      if (jstar < nties) {
+        uint32_t idkey; unsigned long long b1, m1; unsigned int c1, n1;
+        const unsigned int js = static_cast<unsigned int>(jstar);
+        radix_find<kSampleNT, false, false>(
+            as, 20,
+            [&](int i, float sv, uint32_t& key, unsigned long long& w) {
+              if (fkey(sv) != cut_key) return false;
+              key = static_cast<uint32_t>(cid[i]);
+              w = 0;
+              return true;
+            },
+            [&](unsigned long long, unsigned int c) { return c >= js; }, sm, idkey, b1, c1, n1, m1);
+        cut_id = static_cast<int>(idkey);
+      }
     }
   }
+  pc.mark(7);
   const bool minpon = p.min_p > 0.0f;
   const double minq = __dmul_rn(static_cast<double>(fminf(p.min_p, 1.0f)),
                                 static_cast<double>(kMassScale));
-  // final set: drop slots outside top-p / min-p
   unsigned long long S = 0;
   for (int i = threadIdx.x; i < n; i += kSampleNT) {
     const int id = cid[i];
@@ -443,31 +568,96 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
     else cid[i] = -1;
   }
   S = block_sum<kSampleNT>(S, sm);
+  pc.mark(8);
+
+  // (e) draw: first id in index order whose running mass exceeds r
   const unsigned long long r = draw_point(u, S);
-  uint32_t pick; unsigned long long b2, qpick; unsigned int c2, n2;
-  radix_find<kSampleNT, false, true>(
-      as, 20,
-      [&](int i, float, uint32_t& key, unsigned long long& w) {
-        key = static_cast<uint32_t>(cid[i]);
+  const int idbits = 32 - __clz(V > 1 ? V - 1 : 1);
+  const int shift = idbits > 10 ? idbits - 10 : 0;
+  const HistSel hd = hist_round<kSampleNT, 1024, true>(
+      as,
+      [&](int i, float, int& bin, unsigned long long& w) {
         w = mass_of_e(ce[i]);
-        return true;
+        bin = cid[i] >> shift;
+        return w > 0;
       },
-      [&](unsigned long long m, unsigned int) { return m > r; }, sm, pick, b2, c2, n2, qpick);
-  out_id = static_cast<int>(pick);
+      [&](unsigned long long m) { return m > r; }, sm);
+  int pick = -1;
+  unsigned long long qpick = 0;
+  if (hd.bin >= 0) {
+    const int nb = collect_small<kSampleNT>(
+        as,
+        [&](int i, float, unsigned long long& key, unsigned long long& w, int& id) {
+          w = mass_of_e(ce[i]);
+          id = cid[i];
+          if (w == 0 || (id >> shift) != hd.bin) return false;
+          key = static_cast<unsigned long long>(id);
+          return true;
+        },
+        sm);
+    if (nb <= 32) {
+      if (threadIdx.x < 32) {
+        unsigned long long key, w;
+        int id;
+        warp_sorted_pick(nb, hd.before, [&](unsigned long long m) { return m > r; }, sm, key, w, id);
+        if (lane == 0) { sm.sid[0] = id; sm.sel_before = w; }
+      }
+      __syncthreads();
+      pick = sm.sid[0];
+      qpick = sm.sel_before;
+      __syncthreads();
+    }
+  }
+  if (pick < 0) {
+    uint32_t pk; unsigned long long b2, qp; unsigned int c2, n2;
+    radix_find<kSampleNT, false, true>(
+        as, 20,
+        [&](int i, float, uint32_t& key, unsigned long long& w) {
+          key = static_cast<uint32_t>(cid[i]);
+          w = mass_of_e(ce[i]);
+          return true;
+        },
+        [&](unsigned long long m, unsigned int) { return m > r; }, sm, pk, b2, c2, n2, qp);
+    pick = static_cast<int>(pk);
+    qpick = qp;
+  }
+  pc.mark(9);
+  out_id = pick;
   out_prob = __double2float_rn(__ddiv_rn(__ull2double_rn(qpick), __ull2double_rn(S)));
   return true;
 }
 
-// Threshold search on the per-vector maxima of the sample: the rk-th largest,
-// resolved to 16 bits (a lower bound of the exact value).
+// Threshold from the per-vector maxima of the sample: one histogram round over
+// bins of equal width between the largest and the smallest finite maximum,
+// then the smallest maximum inside the bin that holds the rk-th largest (a
+// lower bound of the rk-th largest; -inf when rk exceeds the sample).
 template <int N>
-__device__ __forceinline__ float sample_threshold(const float* vmax, unsigned int rk, BlockScratch& sm) {
-  uint32_t tk; unsigned long long b0, m0; unsigned int c0, n0;
-  radix_find<kSampleNT, true, false>(
-      RegSrc<N>{vmax}, 32,
-      [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; },
-      [&](unsigned long long, unsigned int c) { return c >= rk; }, sm, tk, b0, c0, n0, m0, 16);
-  return key2f(tk);
+__device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm) {
+  float mx = neg_inf(), nmn = neg_inf();
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    mx = fmaxf(mx, vm[i]);
+    if (vm[i] > neg_inf()) nmn = fmaxf(nmn, -vm[i]);
+  }
+  mx = block_max<kSampleNT>(mx, sm);
+  const float mn = -block_max<kSampleNT>(nmn, sm);
+  if (mx == neg_inf()) return neg_inf();
+  const float width = __fsub_rn(mx, mn);
+  const float scale = width > 0.0f ? __fdiv_rn(2046.0f, width) : 0.0f;
+  auto binf = [&](float v) {
+    if (!(v > neg_inf())) return 2047;
+    const int bn = static_cast<int>(__fmul_rn(__fsub_rn(mx, v), scale));
+    return bn > 2046 ? 2046 : bn;
+  };
+  const HistSel hs = hist_round<kSampleNT, 2048, false>(
+      RegSrc<N>{vm}, [&](int, float v, int& bin, unsigned long long& w) { bin = binf(v); w = 1; return true; },
+      [&](unsigned long long c) { return c >= rk; }, sm);
+  if (hs.bin < 0 || hs.bin == 2047) return neg_inf();
+  float nlo = neg_inf();
+#pragma unroll
+  for (int i = 0; i < N; i++)
+    if (binf(vm[i]) == hs.bin) nlo = fmaxf(nlo, -vm[i]);
+  return -block_max<kSampleNT>(nlo, sm);
 }
 
 template <int DT>
@@ -489,6 +679,8 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   const int ht = a.ht_log2 ? (1 << a.ht_log2) : 0;
   int* hval = hkey + ht;
 
+  PhaseClock pc;
+  pc.mark(0);
   const tg_row_params p = a.params[b];
   const char* row = reinterpret_cast<const char*>(a.logits) + b * a.row_stride * E::kSize;
   const float u = a.uniforms ? a.uniforms[b] : 0.0f;
@@ -527,10 +719,23 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
 
   // (a) history -> shared hash of penalised values (raw values read from L2
   // when this runs after the streaming pass)
-  // build_hist(th): penalised values of the distinct history ids; ids whose
-  // penalised value reaches th while the raw one did not are appended to the
-  // candidate list (th = +inf appends nothing).
-  auto build_hist = [&](float th) {
+  // Penalty of one history token (raw value already masked), count c.
+  auto penalise = [&](float y, int c) {
+    if (y == neg_inf()) return y;
+    if (rep_on) y = y > 0.0f ? __fdiv_rn(y, p.repetition_penalty) : __fmul_rn(y, p.repetition_penalty);
+    if (pf_on) y = __fsub_rn(y, __fadd_rn(__fmul_rn(p.frequency_penalty, static_cast<float>(c)), p.presence_penalty));
+    return y;
+  };
+  // Penalties can raise a logit only through a negative presence / frequency.
+  const bool risers = pf_on && (p.presence_penalty < 0.0f || p.frequency_penalty < 0.0f);
+  bool hist_counts_only = false;
+
+  // build_hist(th, values): hash of the distinct history ids with their counts.
+  // With values, every slot also gets its penalised value (raw value read from
+  // global memory) and ids whose penalised value reaches th while the raw one
+  // did not are appended to the candidate list; without, slots keep counts and
+  // the candidate list is penalised from its own raw values.
+  auto build_hist = [&](float th, bool values) {
     if (!need_hist || hist.active) return;
     for (int i = t; i < ht; i += kSampleNT) { hkey[i] = -1; hval[i] = 0; }
     for (int i = t; i < 128; i += kSampleNT) bloom[i] = 0u;
@@ -550,22 +755,20 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
     for (int s = t; s < ht; s += kSampleNT) {
       const int id = hkey[s];
       if (id < 0) continue;
-      const int c = hval[s];
-      float raw = E::load(row, id);
-      if (mask && !mask_allows(mask, id)) raw = neg_inf();
-      float y = raw;
-      if (rep_on) y = y > 0.0f ? __fdiv_rn(y, p.repetition_penalty) : __fmul_rn(y, p.repetition_penalty);
-      if (pf_on) y = __fsub_rn(y, __fadd_rn(__fmul_rn(p.frequency_penalty, static_cast<float>(c)), p.presence_penalty));
-      if (raw == neg_inf()) y = neg_inf();
-      hval[s] = __float_as_int(y);
       const uint32_t hb = (static_cast<uint32_t>(id) * 0x85EBCA77u) >> 20;
       atomicOr(&bloom[hb >> 5], 1u << (hb & 31));
+      if (!values) continue;
+      float raw = E::load(row, id);
+      if (mask && !mask_allows(mask, id)) raw = neg_inf();
+      const float y = penalise(raw, hval[s]);
+      hval[s] = __float_as_int(y);
       if (!(raw >= th) && y >= th) {
         const int pos = atomicAdd(&sm.cand_count, 1);
         if (pos < kCandMax) { cand_y[pos] = y; cand_id[pos] = id; }
       }
     }
     hist.active = 1;
+    hist_counts_only = !values;
     __syncthreads();
   };
 
@@ -579,23 +782,56 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   if (fast) {
     const int keff = greedy ? 1 : (topk ? p.top_k : V);
     const unsigned int need = static_cast<unsigned int>(keff < V ? keff : 1);
-    const float tgt = 2.0f * static_cast<float>(keff) + 128.0f;
+    const float tgt = 1.5f * static_cast<float>(keff) + 96.0f;
+    const int lane = t & 31, warp = t >> 5;
+    const unsigned lt = (1u << lane) - 1u;
+    int* hitidx = reinterpret_cast<int*>(cand_e);  // per-warp lists of hit vectors
+    int wcnt = 0;                                   // this warp's list length (warp-uniform)
 
-    // Append every vector element >= th from vector index j0 on (and the
-    // head / tail scalars when with_scalars) -- the streaming pass.
-    auto collect = [&](float th, int j0, bool with_scalars) {
-      if (with_scalars) {
-        int sc_id = -1;
-        if (t < head) sc_id = t;
-        else if (t - head < V - tail0) sc_id = tail0 + (t - head);
-        float sc = neg_inf();
-        if (sc_id >= 0) {
-          sc = E::load(row, sc_id);
-          if (mask && !mask_allows(mask, sc_id)) sc = neg_inf();
+    auto vmax_of = [&](const uint4& w, int j) {
+      if (!mask) return E::vmax(w);
+      float x[EPV];
+      E::unpack(w, x);
+      const uint32_t bits = mask_bits(mask, head + j * EPV, EPV);
+      float vm = neg_inf();
+#pragma unroll
+      for (int e = 0; e < EPV; e++)
+        if ((bits >> e) & 1u) vm = fmaxf(vm, x[e]);
+      return vm;
+    };
+    // Append the elements >= th of vector j (raw w) to the candidate list.
+    auto append_vec = [&](const uint4& w, int j, float th) {
+      float x[EPV];
+      E::unpack(w, x);
+      const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
+      uint32_t hits = 0;
+#pragma unroll
+      for (int e = 0; e < EPV; e++) hits |= (((bits >> e) & 1u) && x[e] >= th ? 1u : 0u) << e;
+      if (!hits) return;
+      int pos = atomicAdd(&sm.cand_count, __popc(hits));
+#pragma unroll
+      for (int e = 0; e < EPV; e++) {
+        if ((hits >> e) & 1u) {
+          if (pos < kCandMax) { cand_y[pos] = x[e]; cand_id[pos] = head + j * EPV + e; }
+          pos++;
         }
-        warp_append<1, kCandMax>((sc_id >= 0 && sc >= th) ? 1u : 0u, &sc, sc_id, cand_y, cand_id,
-                                 &sm.cand_count);
       }
+    };
+    auto scalars = [&](float th) {
+      int sc_id = -1;
+      if (t < head) sc_id = t;
+      else if (t - head < V - tail0) sc_id = tail0 + (t - head);
+      if (sc_id < 0) return;
+      float sc = E::load(row, sc_id);
+      if (mask && !mask_allows(mask, sc_id)) sc = neg_inf();
+      if (sc >= th) {
+        const int pos = atomicAdd(&sm.cand_count, 1);
+        if (pos < kCandMax) { cand_y[pos] = sc; cand_id[pos] = sc_id; }
+      }
+    };
+    // The streaming pass: one 128-bit load, a vector max and a compare per 16
+    // bytes; a warp ballot records the vectors holding an element >= th.
+    auto scan = [&](float th, int j0) {
       for (int jb = j0; jb < nvec; jb += kUnroll * kSampleNT) {
         uint4 w[kUnroll];
 #pragma unroll
@@ -607,55 +843,47 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
         for (int q = 0; q < kUnroll; q++) {
           if (jb + q * kSampleNT >= nvec) break;  // warp-uniform
           const int j = jb + q * kSampleNT + t;
-          const bool ok = j < nvec;
-          float x[EPV];
-          E::unpack(w[q], x);
-          float vm = neg_inf();
-          if (ok) {
-            if (mask) {
-              const uint32_t bits = mask_bits(mask, head + j * EPV, EPV);
-#pragma unroll
-              for (int e = 0; e < EPV; e++)
-                if (!((bits >> e) & 1u)) x[e] = neg_inf();
+          const bool hit = j < nvec && vmax_of(w[q], j) >= th;
+          const unsigned bal = __ballot_sync(kFull, hit);
+          if (bal) {
+            if (hit) {
+              const int pos = wcnt + __popc(bal & lt);
+              if (pos < kHitCap) hitidx[warp * kHitCap + pos] = j;
             }
-#pragma unroll
-            for (int e = 0; e < EPV; e++) vm = fmaxf(vm, x[e]);
-          }
-          if (ok && vm >= th) {  // rare: only the lanes holding a hit append
-            uint32_t hits = 0;
-#pragma unroll
-            for (int e = 0; e < EPV; e++) hits |= (x[e] >= th ? 1u : 0u) << e;
-            int pos = atomicAdd(&sm.cand_count, __popc(hits));
-#pragma unroll
-            for (int e = 0; e < EPV; e++) {
-              if ((hits >> e) & 1u) {
-                if (pos < kCandMax) { cand_y[pos] = x[e]; cand_id[pos] = head + j * EPV + e; }
-                pos++;
-              }
-            }
+            wcnt += __popc(bal);
           }
         }
       }
+    };
+    // Hit vectors -> candidates (re-read from L2).  False if a list overflowed.
+    auto expand = [&](float th) {
+      if (lane == 0) sm.red_i[warp] = wcnt;
+      __syncthreads();
+      int total = 0;
+      bool over = false;
+#pragma unroll
+      for (int w2 = 0; w2 < kSampleNT / 32; w2++) {
+        const int c = sm.red_i[w2];
+        over |= c > kHitCap;
+        total += c < kHitCap ? c : kHitCap;
+      }
+      for (int f = t; f < total; f += kSampleNT) {
+        int w2 = 0, rem = f;
+        for (;;) {
+          const int c = sm.red_i[w2] < kHitCap ? sm.red_i[w2] : kHitCap;
+          if (rem < c) break;
+          rem -= c;
+          w2++;
+        }
+        const int j = hitidx[w2 * kHitCap + rem];
+        append_vec(__ldg(vrow + j), j, th);
+      }
+      __syncthreads();
+      return !over;
     };
 
     // Sample: the first SV vectors of every thread; their per-vector maxima
     // give the threshold for the rest of the row.
-    auto sample_vmax = [&](uint4* raw, float* vm) {
-#pragma unroll
-      for (int q = 0; q < SV; q++) {
-        const int j = t + q * kSampleNT;
-        vm[q] = neg_inf();
-        if (j < nvec) {
-          raw[q] = ldg_stream(vrow + j);
-          float x[EPV];
-          E::unpack(raw[q], x);
-          const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
-#pragma unroll
-          for (int e = 0; e < EPV; e++)
-            if ((bits >> e) & 1u) vm[q] = fmaxf(vm[q], x[e]);
-        }
-      }
-    };
     const int nsv = nvec < SV * kSampleNT ? nvec : SV * kSampleNT;
     const int sampled = nsv * EPV;
     auto rank_for = [&](float mult) {
@@ -663,45 +891,46 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
                                       static_cast<float>(V)));
       return static_cast<unsigned int>(rr < 1 ? 1 : rr);
     };
-
     float theta = neg_inf();
     unsigned int rk = 0;
+    bool fits;
     {
       uint4 raw[SV];
       float vm[SV];
-      sample_vmax(raw, vm);
-      if (V > kCandMax && sampled > 0) {
-        rk = rank_for(1.0f);
-        theta = rk > static_cast<unsigned int>(nsv) ? neg_inf() : sample_threshold<SV>(vm, rk, sm);
-      }
-      if (t == 0) sm.cand_count = 0;
-      __syncthreads();
+      pc.mark(0);
 #pragma unroll
       for (int q = 0; q < SV; q++) {
         const int j = t + q * kSampleNT;
-        uint32_t hits = 0;
-        float x[EPV];
-        E::unpack(raw[q], x);
+        vm[q] = neg_inf();
         if (j < nvec) {
-          const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
-#pragma unroll
-          for (int e = 0; e < EPV; e++) {
-            if (!((bits >> e) & 1u)) x[e] = neg_inf();
-            hits |= (x[e] >= theta ? 1u : 0u) << e;
-          }
+          raw[q] = ldg_stream(vrow + j);
+          vm[q] = vmax_of(raw[q], j);
         }
-        warp_append<EPV, kCandMax>(hits, x, head + j * EPV, cand_y, cand_id, &sm.cand_count);
+      }
+      if (V > kCandMax && sampled > 0) {
+        rk = rank_for(1.0f);
+        theta = sample_theta<SV>(vm, rk, sm);
+      }
+      if (t == 0) sm.cand_count = 0;
+      __syncthreads();
+      pc.mark(1);
+#pragma unroll
+      for (int q = 0; q < SV; q++) {
+        const int j = t + q * kSampleNT;
+        if (j < nvec && vm[q] >= theta) append_vec(raw[q], j, theta);
       }
     }
-    collect(theta, SV * kSampleNT, true);
-    __syncthreads();
+    scalars(theta);
+    scan(theta, SV * kSampleNT);
+    fits = expand(theta);
+    pc.mark(2);
 
     for (int attempt = 0;; attempt++) {
       if (need_hist) {
-        const int n0 = sm.cand_count < kCandMax ? sm.cand_count : kCandMax;
+        const int n0 = sm.cand_count < kCandMax ? sm.cand_count : kCandMax;  // raw entries
         if (!hist.active) {
-          build_hist(theta);  // appends after n0: those already hold penalised values
-        } else {  // retry: the hash exists; append the risers for the new theta
+          build_hist(theta, risers);  // risers land after n0 with penalised values
+        } else if (risers) {  // retry: append the risers for the new theta
           for (int s = t; s < ht; s += kSampleNT) {
             const int id = hkey[s];
             if (id < 0) continue;
@@ -716,18 +945,21 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
           __syncthreads();
         }
         for (int i = t; i < n0; i += kSampleNT) {  // raw -> penalised for history ids
-          float py;
-          if (hist.find(cand_id[i], py)) cand_y[i] = py;
+          float hv;
+          if (hist.find(cand_id[i], hv))
+            cand_y[i] = hist_counts_only ? penalise(cand_y[i], __float_as_int(hv)) : hv;
         }
         __syncthreads();
       }
+      pc.mark(3);
       const int cnt = sm.cand_count;
-      const bool overflow = cnt > kCandMax;
-      SmemSrc src{cand_y, cand_id, overflow ? kCandMax : cnt, theta};
+      const bool overflow = !fits || cnt > kCandMax;
+      SmemSrc src{cand_y, cand_id, cnt < kCandMax ? cnt : kCandMax, theta};
       const unsigned int nvalid = block_count_if(src, theta, sm);
-      if (t == 0) atomicAdd(&a.counters[5], static_cast<unsigned long long>(cnt));
+      if (t == 0) atomicAdd(&a.counters[5], static_cast<unsigned long long>(nvalid));
+      pc.mark(4);
       if (!overflow && nvalid >= need) {
-        done = finish_cands(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob);
+        done = finish_cands(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob, pc);
         if (done) {
           if (t == 0) atomicAdd(&a.counters[0], 1ull);
           break;
@@ -739,7 +971,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
       if (attempt == kRetries || theta == neg_inf()) break;
       // retry from L2 with a new threshold
       float nt;
-      if (overflow) {  // the tgt-th largest buffered value bounds the k-th from below
+      if (overflow) {  // the tgt-th largest of the buffered values bounds the k-th from below
         uint32_t tk; unsigned long long b0, m0; unsigned int c0, n0;
         const unsigned int tr = static_cast<unsigned int>(tgt);
         radix_find<kSampleNT, true, false>(
@@ -750,25 +982,33 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
         if (!(nt > theta)) nt = neg_inf();
       } else {  // too few: a 4x deeper rank in the sample
         rk = rk * 4u;
-        uint4 raw[SV];
         float vm[SV];
-        sample_vmax(raw, vm);
-        nt = rk > static_cast<unsigned int>(nsv) ? neg_inf() : sample_threshold<SV>(vm, rk, sm);
+#pragma unroll
+        for (int q = 0; q < SV; q++) {
+          const int j = t + q * kSampleNT;
+          vm[q] = j < nvec ? vmax_of(__ldg(vrow + j), j) : neg_inf();
+        }
+        nt = sample_theta<SV>(vm, rk, sm);
         if (!(nt < theta)) nt = neg_inf();
       }
       theta = nt;
       if (V > kCandMax && theta == neg_inf()) break;  // nothing left but the full row
       if (t == 0) sm.cand_count = 0;
+      wcnt = 0;
       __syncthreads();
-      collect(theta, 0, true);
-      __syncthreads();
+      scalars(theta);
+      scan(theta, 0);
+      fits = expand(theta);
+      pc.mark(10);
     }
   }
   if (!done) {
     if (t == 0) atomicAdd(&a.counters[4], 1ull);
-    build_hist(__int_as_float(0x7f800000));
+    if (hist_counts_only) { hist.active = 0; __syncthreads(); }
+    build_hist(__int_as_float(0x7f800000), true);
     GlobalSrc<DT> src{row, V, head, nvec, tail0, mask, hist};
     finish_row(src, p, V, u, false, neg_inf(), sm, out_id, out_prob);
+    pc.mark(11);
   }
   if (t == 0) {
     a.out_ids[b] = out_id;

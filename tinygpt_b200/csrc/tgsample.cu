@@ -352,6 +352,18 @@ int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_
   return TG_OK;
 }
 
+#ifdef TG_PHASE_TIMING
+int32_t tg_debug_phase_cycles(uint64_t* out, int32_t reset) {
+  TG_CUDA(cudaDeviceSynchronize());
+  TG_CUDA(cudaMemcpyFromSymbol(out, tg::g_phase_cycles, sizeof(uint64_t) * 16));
+  if (reset) {
+    static const uint64_t z[16] = {};
+    TG_CUDA(cudaMemcpyToSymbol(tg::g_phase_cycles, z, sizeof(z)));
+  }
+  return TG_OK;
+}
+#endif
+
 int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits) {
   if (!s || !out_bits) return fail(TG_ERR_INVALID_ARG, "NULL argument");
   DeviceGuard g(s->device);
