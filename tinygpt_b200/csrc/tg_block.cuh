@@ -47,6 +47,22 @@ __device__ __forceinline__ float block_max(float v, BlockScratch& sm) {
   return r;
 }
 
+// Two maxima with one pair of barriers.
+template <int NT>
+__device__ __forceinline__ void block_max2(float& a, float& b, BlockScratch& sm) {
+  for (int o = 16; o > 0; o >>= 1) {
+    a = fmaxf(a, __shfl_xor_sync(kFull, a, o));
+    b = fmaxf(b, __shfl_xor_sync(kFull, b, o));
+  }
+  if ((threadIdx.x & 31) == 0) { sm.red_f[threadIdx.x >> 5] = a; sm.red_f2[threadIdx.x >> 5] = b; }
+  __syncthreads();
+  a = sm.red_f[0];
+  b = sm.red_f2[0];
+#pragma unroll
+  for (int i = 1; i < NT / 32; i++) { a = fmaxf(a, sm.red_f[i]); b = fmaxf(b, sm.red_f2[i]); }
+  __syncthreads();
+}
+
 template <int NT>
 __device__ __forceinline__ unsigned long long block_sum(unsigned long long v, BlockScratch& sm) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
@@ -159,26 +175,32 @@ struct HistSel {
   unsigned long long in_bin;
 };
 
-template <int NT, int NB, bool kMass, class Src, class BinW, class Reached>
-__device__ HistSel hist_round(const Src& src, BinW binw, Reached reached, BlockScratch& sm) {
+// hist_zero + (caller's pass calling hist_put) + hist_scan is a hist_round
+// whose accumulation rides inside another pass over the data.  The caller
+// synchronizes between hist_zero and the first hist_put.
+template <int NT, int NB, bool kMass>
+__device__ __forceinline__ void hist_zero(BlockScratch& sm) {
   static_assert(NB % NT == 0, "bins must be a multiple of the block");
   static_assert(kMass ? NB <= 1024 : NB <= 2048, "histogram does not fit");
   constexpr int P = NB / NT;
-  const int t = threadIdx.x;
 #pragma unroll
   for (int j = 0; j < P; j++) {
-    if (kMass) sm.hm[t * P + j] = 0ull;
-    else sm.hc[t * P + j] = 0u;
+    if (kMass) sm.hm[threadIdx.x * P + j] = 0ull;
+    else sm.hc[threadIdx.x * P + j] = 0u;
   }
-  if (t == 0) sm.sel_bin = 0xffffffffu;
-  __syncthreads();
-  src.for_each([&](int i, float y) {
-    int bin;
-    unsigned long long w;
-    if (!binw(i, y, bin, w)) return;
-    if (kMass) atomicAdd(&sm.hm[bin], w);
-    else atomicAdd(&sm.hc[bin], 1u);
-  });
+  if (threadIdx.x == 0) sm.sel_bin = 0xffffffffu;
+}
+
+template <bool kMass>
+__device__ __forceinline__ void hist_put(BlockScratch& sm, int bin, unsigned long long w) {
+  if (kMass) atomicAdd(&sm.hm[bin], w);
+  else atomicAdd(&sm.hc[bin], 1u);
+}
+
+template <int NT, int NB, bool kMass, class Reached>
+__device__ HistSel hist_scan(Reached reached, BlockScratch& sm) {
+  constexpr int P = NB / NT;
+  const int t = threadIdx.x;
   __syncthreads();
   unsigned long long v[P];
   unsigned long long loc = 0;
@@ -206,6 +228,18 @@ __device__ HistSel hist_round(const Src& src, BinW binw, Reached reached, BlockS
   HistSel r{static_cast<int>(sm.sel_bin), sm.sel_before, sm.sel_mass};  // bin -1: not reached
   __syncthreads();
   return r;
+}
+
+template <int NT, int NB, bool kMass, class Src, class BinW, class Reached>
+__device__ HistSel hist_round(const Src& src, BinW binw, Reached reached, BlockScratch& sm) {
+  hist_zero<NT, NB, kMass>(sm);
+  __syncthreads();
+  src.for_each([&](int i, float y) {
+    int bin;
+    unsigned long long w;
+    if (binw(i, y, bin, w)) hist_put<kMass>(sm, bin, w);
+  });
+  return hist_scan<NT, NB, kMass>(reached, sm);
 }
 
 // Collect the elements for which member(i, y, key, w, id) holds into the small

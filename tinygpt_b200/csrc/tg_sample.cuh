@@ -38,7 +38,10 @@ constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold 
 #endif
 constexpr int kUnroll = TG_UNROLL;  // 128-bit loads in flight per thread
 constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) before the full row
-constexpr int kMinCtasPerSm = 4; // occupancy target (caps registers at 64)
+#ifndef TG_MIN_CTAS
+#define TG_MIN_CTAS 4
+#endif
+constexpr int kMinCtasPerSm = TG_MIN_CTAS;  // occupancy target (4: registers capped at 64)
 constexpr int kHitCap = kCandMax / (kSampleNT / 32);  // hit vectors listed per warp
 
 // Diagnostic build only (-DTG_PHASE_TIMING): cycles per phase summed over CTAs.
@@ -363,8 +366,8 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
     ymax = fmaxf(ymax, y);
     if (y > neg_inf()) nymin = fmaxf(nymin, -y);
   });
-  ymax = block_max<kSampleNT>(ymax, sm);
-  const float ymin = -block_max<kSampleNT>(nymin, sm);
+  block_max2<kSampleNT>(ymax, nymin, sm);
+  const float ymin = -nymin;
   if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
 
   float sk = neg_inf();
@@ -429,7 +432,15 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
   pc.mark(5);
   const float smax = __fdiv_rn(ymax, T);
 
-  // compaction: s, e in place; ids of dropped slots set to -1
+  // compaction: s, e in place; ids of dropped slots set to -1.  The same pass
+  // fills the top-p mass histogram over d = smax - s (32 bins per unit of s).
+  const bool toppon = p.top_p < 1.0f;
+  auto dbin = [&](float sv) {
+    const int bn = static_cast<int>(__fmul_rn(__fsub_rn(smax, sv), 32.0f));
+    return bn > 1023 ? 1023 : bn;
+  };
+  if (toppon) hist_zero<kSampleNT, 1024, true>(sm);
+  __syncthreads();
   unsigned long long Q = 0;
   for (int i = threadIdx.x; i < n; i += kSampleNT) {
     const float y = cy[i];
@@ -442,7 +453,9 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
     if (keep) {
       const float d = __fsub_rn(sv, smax);
       e = d >= -32.0f ? tg_exp(d) : 0.0f;
-      Q += mass_of_e(e);
+      const unsigned long long q = mass_of_e(e);
+      Q += q;
+      if (toppon && q > 0) hist_put<true>(sm, dbin(sv), q);
       cy[i] = sv;
       ce[i] = e;
     } else {
@@ -455,24 +468,13 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
 
   // (d) top-p: the last element (cut_key, cut_id) of the shortest prefix in
   // (s desc, id asc) order whose mass reaches top_p * Q.
-  const bool toppon = p.top_p < 1.0f;
   uint32_t cut_key = 0;
   int cut_id = 0x7fffffff;
   if (toppon) {
     const double tau = __dmul_rn(static_cast<double>(p.top_p), __ull2double_rn(Q));
-    auto dbin = [&](float sv) {
-      const int bn = static_cast<int>(__fmul_rn(__fsub_rn(smax, sv), 32.0f));
-      return bn > 1023 ? 1023 : bn;
-    };
     bool resolved = false;
     if (tau > 0.0) {
-      const HistSel hs = hist_round<kSampleNT, 1024, true>(
-          as,
-          [&](int i, float sv, int& bin, unsigned long long& w) {
-            w = mass_of_e(ce[i]);
-            bin = dbin(sv);
-            return w > 0;
-          },
+      const HistSel hs = hist_scan<kSampleNT, 1024, true>(
           [&](unsigned long long m) { return __ull2double_rn(m) >= tau; }, sm);
       if (hs.bin >= 0) {
         const int nb = collect_small<kSampleNT>(
@@ -553,7 +555,11 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
   const bool minpon = p.min_p > 0.0f;
   const double minq = __dmul_rn(static_cast<double>(fminf(p.min_p, 1.0f)),
                                 static_cast<double>(kMassScale));
-  unsigned long long S = 0;
+  const int idbits = 32 - __clz(V > 1 ? V - 1 : 1);
+  const int shift = idbits > 10 ? idbits - 10 : 0;
+  hist_zero<kSampleNT, 1024, true>(sm);
+  __syncthreads();
+  unsigned long long S = 0;  // the same pass fills the draw histogram over id bins
   for (int i = threadIdx.x; i < n; i += kSampleNT) {
     const int id = cid[i];
     if (id < 0) continue;
@@ -564,24 +570,19 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       keep = k > cut_key || (k == cut_key && id <= cut_id);
     }
     if (keep && minpon) keep = __ull2double_rn(q) >= minq;
-    if (keep) S += q;
-    else cid[i] = -1;
+    if (keep) {
+      S += q;
+      if (q > 0) hist_put<true>(sm, id >> shift, q);
+    } else {
+      cid[i] = -1;
+    }
   }
   S = block_sum<kSampleNT>(S, sm);
   pc.mark(8);
 
   // (e) draw: first id in index order whose running mass exceeds r
   const unsigned long long r = draw_point(u, S);
-  const int idbits = 32 - __clz(V > 1 ? V - 1 : 1);
-  const int shift = idbits > 10 ? idbits - 10 : 0;
-  const HistSel hd = hist_round<kSampleNT, 1024, true>(
-      as,
-      [&](int i, float, int& bin, unsigned long long& w) {
-        w = mass_of_e(ce[i]);
-        bin = cid[i] >> shift;
-        return w > 0;
-      },
-      [&](unsigned long long m) { return m > r; }, sm);
+  const HistSel hd = hist_scan<kSampleNT, 1024, true>([&](unsigned long long m) { return m > r; }, sm);
   int pick = -1;
   unsigned long long qpick = 0;
   if (hd.bin >= 0) {
@@ -639,8 +640,8 @@ __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm
     mx = fmaxf(mx, vm[i]);
     if (vm[i] > neg_inf()) nmn = fmaxf(nmn, -vm[i]);
   }
-  mx = block_max<kSampleNT>(mx, sm);
-  const float mn = -block_max<kSampleNT>(nmn, sm);
+  block_max2<kSampleNT>(mx, nmn, sm);
+  const float mn = -nmn;
   if (mx == neg_inf()) return neg_inf();
   const float width = __fsub_rn(mx, mn);
   const float scale = width > 0.0f ? __fdiv_rn(2046.0f, width) : 0.0f;
@@ -901,11 +902,14 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
 #pragma unroll
       for (int q = 0; q < SV; q++) {
         const int j = t + q * kSampleNT;
-        vm[q] = neg_inf();
-        if (j < nvec) {
-          raw[q] = ldg_stream(vrow + j);
-          vm[q] = vmax_of(raw[q], j);
-        }
+        if (j < nvec) raw[q] = ldg_stream(vrow + j);
+      }
+      // the history hash (counts only) is built while the sample loads fly
+      if (!risers) build_hist(0.0f, false);
+#pragma unroll
+      for (int q = 0; q < SV; q++) {
+        const int j = t + q * kSampleNT;
+        vm[q] = j < nvec ? vmax_of(raw[q], j) : neg_inf();
       }
       if (V > kCandMax && sampled > 0) {
         rk = rank_for(1.0f);
@@ -960,6 +964,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
       pc.mark(4);
       if (!overflow && nvalid >= need) {
         done = finish_cands(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob, pc);
+        pc.mark(9);
         if (done) {
           if (t == 0) atomicAdd(&a.counters[0], 1ull);
           break;
