@@ -42,7 +42,8 @@ constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) befo
 #define TG_MIN_CTAS 4
 #endif
 constexpr int kMinCtasPerSm = TG_MIN_CTAS;  // occupancy target (4: registers capped at 64)
-constexpr int kHitCap = kCandMax / (kSampleNT / 32);  // hit vectors listed per warp
+constexpr int kRing = 64;  // hit-vector ring entries per warp (drained at 32)
+static_assert((kSampleNT / 32) * kRing * 20 <= kCandMax * 4, "rings must fit in cand_e");
 
 // Diagnostic build only (-DTG_PHASE_TIMING): cycles per phase summed over CTAs.
 #ifdef TG_PHASE_TIMING
@@ -669,7 +670,6 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ BlockScratch sm;
   __shared__ uint32_t bloom[128];
-
   const int b = blockIdx.x;
   const int t = threadIdx.x;
   const int V = a.vocab;
@@ -786,8 +786,6 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
     const float tgt = 1.5f * static_cast<float>(keff) + 96.0f;
     const int lane = t & 31, warp = t >> 5;
     const unsigned lt = (1u << lane) - 1u;
-    int* hitidx = reinterpret_cast<int*>(cand_e);  // per-warp lists of hit vectors
-    int wcnt = 0;                                   // this warp's list length (warp-uniform)
 
     auto vmax_of = [&](const uint4& w, int j) {
       if (!mask) return E::vmax(w);
@@ -830,9 +828,50 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
         if (pos < kCandMax) { cand_y[pos] = sc; cand_id[pos] = sc_id; }
       }
     };
+    // Per-warp ring of hit vectors (raw 16 bytes + vector index) in the bytes
+    // of cand_e, which stage (b) only needs later.  A warp drains its ring
+    // itself whenever it holds >= 32 entries: lane i expands entries i, i+32.
+    uint4* rdata = reinterpret_cast<uint4*>(cand_e) + warp * kRing;
+    int* ridx = reinterpret_cast<int*>(reinterpret_cast<uint4*>(cand_e) + (kSampleNT / 32) * kRing) + warp * kRing;
+    auto drain = [&](int cnt, float th) {  // warp-uniform cnt <= kRing
+      __syncwarp();
+      for (int i0 = 0; i0 < cnt; i0 += 32) {
+        const int i = i0 + lane;
+        float x[EPV];
+        uint32_t hits = 0;
+        int j = 0;
+        if (i < cnt) {
+          j = ridx[i];
+          E::unpack(rdata[i], x);
+          const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
+#pragma unroll
+          for (int e = 0; e < EPV; e++) hits |= (((bits >> e) & 1u) && x[e] >= th ? 1u : 0u) << e;
+        }
+        const int c = __popc(hits);
+        int pre = 0, tot = 0;
+#pragma unroll
+        for (int bit = 0; bit < (EPV >= 8 ? 4 : 3); bit++) {
+          const unsigned m = __ballot_sync(kFull, (c >> bit) & 1);
+          pre += __popc(m & lt) << bit;
+          tot += __popc(m) << bit;
+        }
+        int base = 0;
+        if (lane == 0 && tot) base = atomicAdd(&sm.cand_count, tot);
+        int pos = __shfl_sync(kFull, base, 0) + pre;
+#pragma unroll
+        for (int e = 0; e < EPV; e++) {
+          if ((hits >> e) & 1u) {
+            if (pos < kCandMax) { cand_y[pos] = x[e]; cand_id[pos] = head + j * EPV + e; }
+            pos++;
+          }
+        }
+      }
+      __syncwarp();
+    };
     // The streaming pass: one 128-bit load, a vector max and a compare per 16
-    // bytes; a warp ballot records the vectors holding an element >= th.
+    // bytes; a warp ballot sends the vectors holding an element >= th to the ring.
     auto scan = [&](float th, int j0) {
+      int rcnt = 0;  // warp-uniform ring fill
       for (int jb = j0; jb < nvec; jb += kUnroll * kSampleNT) {
         uint4 w[kUnroll];
 #pragma unroll
@@ -848,39 +887,20 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
           const unsigned bal = __ballot_sync(kFull, hit);
           if (bal) {
             if (hit) {
-              const int pos = wcnt + __popc(bal & lt);
-              if (pos < kHitCap) hitidx[warp * kHitCap + pos] = j;
+              const int pos = rcnt + __popc(bal & lt);
+              rdata[pos] = w[q];
+              ridx[pos] = j;
             }
-            wcnt += __popc(bal);
+            rcnt += __popc(bal);
+            if (rcnt >= 32) { drain(rcnt, th); rcnt = 0; }
           }
         }
       }
+      if (rcnt) drain(rcnt, th);
     };
-    // Hit vectors -> candidates (re-read from L2).  False if a list overflowed.
-    auto expand = [&](float th) {
-      if (lane == 0) sm.red_i[warp] = wcnt;
+    auto expand = [&](float) {
       __syncthreads();
-      int total = 0;
-      bool over = false;
-#pragma unroll
-      for (int w2 = 0; w2 < kSampleNT / 32; w2++) {
-        const int c = sm.red_i[w2];
-        over |= c > kHitCap;
-        total += c < kHitCap ? c : kHitCap;
-      }
-      for (int f = t; f < total; f += kSampleNT) {
-        int w2 = 0, rem = f;
-        for (;;) {
-          const int c = sm.red_i[w2] < kHitCap ? sm.red_i[w2] : kHitCap;
-          if (rem < c) break;
-          rem -= c;
-          w2++;
-        }
-        const int j = hitidx[w2 * kHitCap + rem];
-        append_vec(__ldg(vrow + j), j, th);
-      }
-      __syncthreads();
-      return !over;
+      return true;
     };
 
     // Sample: the first SV vectors of every thread; their per-vector maxima
@@ -999,7 +1019,6 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
       theta = nt;
       if (V > kCandMax && theta == neg_inf()) break;  // nothing left but the full row
       if (t == 0) sm.cand_count = 0;
-      wcnt = 0;
       __syncthreads();
       scalars(theta);
       scan(theta, 0);
