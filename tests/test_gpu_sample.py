@@ -152,3 +152,23 @@ def test_host_entry_point_matches_device_entry_point(oracle_mod, sampler_factory
     oi, op = oracle_mod.sample(w["logits"], w["params"], w["history"], w["history_len"], None,
                                None, w["uniforms"])
     assert np.array_equal(hi, oi) and np.array_equal(hp.view(np.uint32), op.view(np.uint32))
+
+
+@pytest.mark.parametrize("scale", [0.05, 0.3, 3.0])
+def test_no_topk_truncation_modes(oracle_mod, sampler_factory, scale):
+    """Rows without top-k but with top-p and/or min-p: the candidate list holds
+    the largest values only, the rest contributes its mass; flat rows make the
+    top-p prefix run past the list (full-row path) unless min-p stops it."""
+    V = 32000
+    B = 48
+    w, g = _base(B, V, int(scale * 100) + 7, "bf16", scale=scale)
+    p = w["params"]
+    p["temperature"] = g.choice([0.5, 1.0, 2.0], size=B)
+    p["top_k"] = 0
+    p["top_p"] = g.choice([1.0, 0.99, 0.9, 0.5], size=B)
+    p["min_p"] = g.choice([0.0, 0.05, 0.5, 0.9], size=B)
+    w["history"] = g.integers(0, V, size=(B, 64)).astype(np.int32)
+    w["history_len"] = np.full(B, 64, np.int32)
+    p["presence_penalty"] = 0.4
+    p["frequency_penalty"] = 0.2
+    assert_same(oracle_mod, sampler_factory(V), w, what=f"no-topk scale={scale}")

@@ -37,6 +37,7 @@ constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold 
 #define TG_UNROLL 4
 #endif
 constexpr int kUnroll = TG_UNROLL;  // 128-bit loads in flight per thread
+constexpr int kNoTopkTarget = 512;  // candidate target of rows without top-k
 constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) before the full row
 #ifndef TG_MIN_CTAS
 #define TG_MIN_CTAS 4
@@ -353,9 +354,14 @@ __device__ __forceinline__ unsigned long long mass_of_e(float e) {
 // function; the crossing bin is then resolved exactly by one warp (<= 32
 // members, the common case) or by the radix version above.  Returns false when
 // an element below theta could survive top-k (the caller lowers theta).
+// partial: the row has no top-k and the list holds only the elements >= theta;
+// q_rest is then the exact mass of every other finite element.  The row can be
+// finished from the list when the top-p cut falls inside it, or when min-p
+// provably drops everything below theta; otherwise false.
 __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
                              const tg_row_params& p, int V, float u, BlockScratch& sm,
-                             int& out_id, float& out_prob, PhaseClock& pc) {
+                             int& out_id, float& out_prob, PhaseClock& pc, bool partial = false,
+                             unsigned long long q_rest = 0) {
   SmemSrc src{cy, cid, n, theta};
   if (!(p.temperature > 0.0f)) return finish_row(src, p, V, u, false, theta, sm, out_id, out_prob);
   const float T = p.temperature;
@@ -369,7 +375,10 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
   });
   block_max2<kSampleNT>(ymax, nymin, sm);
   const float ymin = -nymin;
-  if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
+  if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return !partial; }
+  const float below = key2f(fkey(theta) - 1u);  // largest value absent from the list
+  // elements below theta must come strictly after the list in (s desc) order
+  if (partial && __fdiv_rn(below, T) >= __fdiv_rn(ymin, T)) return false;
 
   float sk = neg_inf();
   if (topk) {
@@ -428,10 +437,18 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       }
     }
     sk = __fdiv_rn(key2f(kkey), T);
-    if (theta > neg_inf() && __fdiv_rn(key2f(fkey(theta) - 1u), T) >= sk) return false;
+    if (theta > neg_inf() && __fdiv_rn(below, T) >= sk) return false;
   }
   pc.mark(5);
   const float smax = __fdiv_rn(ymax, T);
+  const bool minpon = p.min_p > 0.0f;
+  const double minq = __dmul_rn(static_cast<double>(fminf(p.min_p, 1.0f)),
+                                static_cast<double>(kMassScale));
+  // partial rows: whether min-p drops every element below theta (tg_exp is
+  // within one ulp of exp, hence the small relative margin)
+  const bool minp_excludes_rest =
+      minpon && __dadd_rn(__dmul_rn(__ull2double_rn(qmass(__fsub_rn(__fdiv_rn(below, T), smax))), 1.000001), 1.0) < minq;
+  if (partial && p.top_p >= 1.0f && !minp_excludes_rest) return false;
 
   // compaction: s, e in place; ids of dropped slots set to -1.  The same pass
   // fills the top-p mass histogram over d = smax - s (32 bins per unit of s).
@@ -463,7 +480,7 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       cid[i] = -1;
     }
   }
-  Q = block_sum<kSampleNT>(Q, sm);
+  Q = block_sum<kSampleNT>(Q, sm) + q_rest;
   ASrc as{cy, cid, n};
   pc.mark(6);
 
@@ -502,6 +519,11 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
           __syncthreads();
           resolved = true;
         }
+      } else if (partial) {  // the prefix runs past the list
+        if (!minp_excludes_rest) return false;
+        cut_key = 0u;  // every list element is inside the prefix
+        cut_id = 0x7fffffff;
+        resolved = true;
       }
     } else {  // top_p <= 0: the single top element (smallest id among the maxima)
       cut_key = fkey(smax);
@@ -553,9 +575,6 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
     }
   }
   pc.mark(7);
-  const bool minpon = p.min_p > 0.0f;
-  const double minq = __dmul_rn(static_cast<double>(fminf(p.min_p, 1.0f)),
-                                static_cast<double>(kMassScale));
   const int idbits = 32 - __clz(V > 1 ? V - 1 : 1);
   const int shift = idbits > 10 ? idbits - 10 : 0;
   hist_zero<kSampleNT, 1024, true>(sm);
@@ -775,7 +794,10 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
 
   const bool greedy = !(p.temperature > 0.0f);
   const bool topk = p.top_k > 0 && p.top_k < V;
-  const bool fast = greedy || (topk && p.top_k <= kFastMaxK) || V <= kCandMax;
+  // rows without top-k but with top-p / min-p: the list holds the largest
+  // ~kNoTopkTarget values and the rest of the row contributes its mass only
+  const bool truncated = p.top_p < 1.0f || p.min_p > 0.0f;
+  const bool fast = greedy || (topk && p.top_k <= kFastMaxK) || V <= kCandMax || (!topk && truncated);
   int out_id = -1;
   float out_prob = 0.0f;
   bool done = false;
@@ -783,7 +805,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   if (fast) {
     const int keff = greedy ? 1 : (topk ? p.top_k : V);
     const unsigned int need = static_cast<unsigned int>(keff < V ? keff : 1);
-    const float tgt = 1.5f * static_cast<float>(keff) + 96.0f;
+    const float tgt = 1.5f * static_cast<float>(keff < V ? keff : kNoTopkTarget) + 96.0f;
     const int lane = t & 31, warp = t >> 5;
     const unsigned lt = (1u << lane) - 1u;
 
@@ -983,7 +1005,40 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
       if (t == 0) atomicAdd(&a.counters[5], static_cast<unsigned long long>(nvalid));
       pc.mark(4);
       if (!overflow && nvalid >= need) {
-        done = finish_cands(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob, pc);
+        const bool partial = !greedy && !topk && theta > neg_inf();
+        unsigned long long qrest = 0;
+        if (partial) {  // exact mass of every finite element below theta (row re-read from L2)
+          float ym = neg_inf();
+          src.for_each([&](int, float y) { ym = fmaxf(ym, y); });
+          ym = block_max<kSampleNT>(ym, sm);
+          const float T = p.temperature;
+          const float smax = __fdiv_rn(ym, T);
+          auto rest = [&](int v, float y) {
+            float hv;
+            if (hist.active && hist.find(v, hv)) y = hist_counts_only ? penalise(y, __float_as_int(hv)) : hv;
+            return (y < theta && y > neg_inf()) ? qmass(__fsub_rn(__fdiv_rn(y, T), smax)) : 0ull;
+          };
+          if (t < head) {
+            float y = E::load(row, t);
+            if (mask && !mask_allows(mask, t)) y = neg_inf();
+            qrest += rest(t, y);
+          }
+          if (t < V - tail0) {
+            float y = E::load(row, tail0 + t);
+            if (mask && !mask_allows(mask, tail0 + t)) y = neg_inf();
+            qrest += rest(tail0 + t, y);
+          }
+          for (int j = t; j < nvec; j += kSampleNT) {
+            float x[EPV];
+            E::unpack(__ldg(vrow + j), x);
+            const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
+#pragma unroll
+            for (int e = 0; e < EPV; e++) qrest += rest(head + j * EPV + e, ((bits >> e) & 1u) ? x[e] : neg_inf());
+          }
+          qrest = block_sum<kSampleNT>(qrest, sm);
+        }
+        done = finish_cands(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob, pc,
+                            partial, qrest);
         pc.mark(9);
         if (done) {
           if (t == 0) atomicAdd(&a.counters[0], 1ull);
