@@ -130,8 +130,17 @@ def profile_traffic():
         return None
 
 
+def use_all_host_threads() -> int:
+    """The oracle's OpenMP pool sized to every host core (torchrun sets
+    OMP_NUM_THREADS=1 per rank); must run before the oracle library loads."""
+    n = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    return n
+
+
 def cpu_baseline(rows_logits_bf16: np.ndarray, p, hist, hlen, u, budget_s=10.0):
     """The oracle on the host cores over repeated bounded samples of the workload."""
+    use_all_host_threads()
     from oracle import oracle
     oracle.build()
     n = rows_logits_bf16.shape[0]
@@ -148,11 +157,11 @@ def cpu_baseline(rows_logits_bf16: np.ndarray, p, hist, hlen, u, budget_s=10.0):
 def run_reference(args, rank, world):
     if rank != 0:
         return
+    cores = use_all_host_threads()
     from tinygpt_b200 import workloads as W
     w = W.make(4, seed=1, batch=512)
     from oracle import oracle
     oracle.build()
-    cores = os.cpu_count()
     step = lambda: oracle.sample(w["logits"], w["params"], w["history"], w["history_len"], None,  # noqa: E731
                                  None, w["uniforms"])
     for _ in range(args.warmup):
