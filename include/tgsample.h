@@ -176,9 +176,52 @@ int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_
                               const float* u_draw, int32_t* out_ids, int32_t* out_n,
                               void* stream);
 
+/* ---- vocab-sharded mode (one process per GPU, each owning a vocab slice) ----
+ * For vocabularies or batches where one GPU should not hold whole rows: rank r
+ * holds ids [vocab_offset, vocab_offset + vocab) of every row (vocab = the
+ * handle's vocab).  tg_sample_shard_local writes one record per row: the local
+ * survivors of top-k (every local value >= the local k-th, ties kept, global
+ * ids) or, for greedy rows, the local first maximum.  The caller all-gathers the
+ * records of all ranks (e.g. ncclAllGather / torch.distributed over NVLink) into
+ * [nshards][batch] order and every rank calls tg_sample_shard_merge, which
+ * returns exactly what tg_sample returns on the whole rows.  Supported rows:
+ * greedy, or 0 < top_k <= 1024 (others: id -1 and device status bit 2).
+ * No counterpart call exists in the reference (its sampler is single-device);
+ * the semantics are those of tg_sample. */
+#define TG_SHARD_CAP 1280
+typedef struct tg_shard_cand { float value; int32_t id; } tg_shard_cand;
+typedef struct tg_shard_record {
+  int32_t count;   /* entries in cand; -1: row not supported in sharded mode */
+  int32_t flags;   /* bit 0: more than TG_SHARD_CAP local survivors        */
+  float absent_max; /* an upper bound of the local values not in cand     */
+  int32_t reserved;
+  tg_shard_cand cand[TG_SHARD_CAP];
+} tg_shard_record;
+
+/* Local half: arguments as tg_sample for this rank's slice (history ids and
+ * mask bit positions are global; mask_table rows span full_vocab bits).
+ * out_records: [batch] device records. */
+int32_t tg_sample_shard_local(tg_sampler* s, int32_t vocab_offset, int32_t full_vocab,
+                              const void* logits, int32_t dtype, int64_t row_stride,
+                              int32_t batch, const tg_row_params* params,
+                              const int32_t* history, const int32_t* history_len,
+                              int32_t history_stride, const uint32_t* mask_table,
+                              int32_t num_states, const int32_t* state_id,
+                              tg_shard_record* out_records, void* stream);
+
+/* Merge half: records [nshards][batch] (gathered), the same params and
+ * uniforms on every rank; writes ids / probabilities as tg_sample.  The handle
+ * needs max_batch >= batch (its vocab is not used). */
+int32_t tg_sample_shard_merge(tg_sampler* s, const tg_shard_record* records, int32_t nshards,
+                              int32_t full_vocab, int32_t batch, const tg_row_params* params,
+                              const float* uniforms, int32_t* out_ids, float* out_probs,
+                              void* stream);
+
 /* Device error word of the last completed call on this handle (synchronizes
  * the handle's device).  Bit 0: a state_id outside [0, num_states);
- * bit 1: a draft id outside [0, vocab).  Cleared by this call. */
+ * bit 1: a draft id outside [0, vocab); bit 2: a row the vocab-sharded mode
+ * could not resolve (unsupported parameters, more than TG_SHARD_CAP local
+ * survivors, or a top-k threshold tie between shards).  Cleared by this call. */
 int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits);
 
 /* Per-handle path counters of tg_sample (diagnostics, the device-side analogue

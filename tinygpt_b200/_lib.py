@@ -24,6 +24,8 @@ TG_DTYPE_BF16 = 1
 TG_MAX_VOCAB = 1 << 20
 TG_MAX_HISTORY = 4096
 TG_STATIC_SPEC_MAX_ROWS = 8192
+TG_SHARD_CAP = 1280
+SHARD_RECORD_BYTES = 16 + 8 * TG_SHARD_CAP
 
 ROW_PARAMS_DTYPE = np.dtype([
     ("temperature", np.float32), ("top_p", np.float32), ("min_p", np.float32),
@@ -33,7 +35,7 @@ ROW_PARAMS_DTYPE = np.dtype([
 
 EXPORTED = ["tg_abi_version", "tg_last_error_string", "tg_sampler_create", "tg_sampler_destroy",
             "tg_sample", "tg_sample_host", "tg_spec_verify", "tg_sampler_device_status", "tg_sampler_path_counters",
-            "tg_spec_verify_static"]
+            "tg_spec_verify_static", "tg_sample_shard_local", "tg_sample_shard_merge"]
 
 
 class TGError(RuntimeError):
@@ -75,6 +77,11 @@ def load(path: str = LIB_PATH):
     L.tg_sampler_path_counters.restype = i32
     L.tg_spec_verify_static.argtypes = [i32, i32, vp, vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]
     L.tg_spec_verify_static.restype = i32
+    L.tg_sample_shard_local.argtypes = [vp, i32, i32, vp, i32, i64, i32, vp, vp, vp, i32, vp, i32,
+                                        vp, vp, vp]
+    L.tg_sample_shard_local.restype = i32
+    L.tg_sample_shard_merge.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp, vp, vp]
+    L.tg_sample_shard_merge.restype = i32
     _LIB = L
     return L
 

@@ -85,6 +85,11 @@ struct SampleArgs {
   float* out_probs;
   uint32_t* status;
   unsigned long long* counters;  // TG_PATH_* counters
+  // vocab-sharded mode: this call sees ids [vocab_offset, vocab_offset + vocab)
+  // of rows of full_vocab ids and writes one record per row instead of ids
+  int32_t vocab_offset;
+  int32_t full_vocab;
+  tg_shard_record* shard_out;
 };
 
 // History hash in shared memory: key = token id (-1 empty); val = count, then
@@ -121,13 +126,14 @@ struct GlobalSrc {
   int V, head, nvec, tail0;
   const uint32_t* mask;
   Hist hist;
+  int moff;  // bit offset of element 0 in the mask row (vocab shards)
   template <class F>
   __device__ __forceinline__ void for_each(F&& f) const {
     using E = Elt<DT>;
     constexpr int EPV = E::kEPV;
     auto one = [&](int v, float x) {
       float y;
-      if (!hist.find(v, y)) y = (mask && !mask_allows(mask, v)) ? neg_inf() : x;
+      if (!hist.find(v, y)) y = (mask && !mask_allows(mask, v + moff)) ? neg_inf() : x;
       f(v, y);
     };
     const int t = threadIdx.x;
@@ -138,7 +144,7 @@ struct GlobalSrc {
       float x[EPV];
       E::unpack(__ldg(vrow + j), x);
       const int e0 = head + j * EPV;
-      const uint32_t bits = mask ? mask_bits(mask, e0, EPV) : 0xffu;
+      const uint32_t bits = mask ? mask_bits(mask, e0 + moff, EPV) : 0xffu;
 #pragma unroll
       for (int e = 0; e < EPV; e++) {
         float y;
@@ -361,7 +367,8 @@ __device__ __forceinline__ unsigned long long mass_of_e(float e) {
 __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
                              const tg_row_params& p, int V, float u, BlockScratch& sm,
                              int& out_id, float& out_prob, PhaseClock& pc, bool partial = false,
-                             unsigned long long q_rest = 0) {
+                             unsigned long long q_rest = 0, float below_override = 0.0f,
+                             bool use_below = false) {
   SmemSrc src{cy, cid, n, theta};
   if (!(p.temperature > 0.0f)) return finish_row(src, p, V, u, false, theta, sm, out_id, out_prob);
   const float T = p.temperature;
@@ -376,7 +383,8 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
   block_max2<kSampleNT>(ymax, nymin, sm);
   const float ymin = -nymin;
   if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return !partial; }
-  const float below = key2f(fkey(theta) - 1u);  // largest value absent from the list
+  // an upper bound of the values absent from the list
+  const float below = use_below ? below_override : key2f(fkey(theta) - 1u);
   // elements below theta must come strictly after the list in (s desc) order
   if (partial && __fdiv_rn(below, T) >= __fdiv_rn(ymin, T)) return false;
 
@@ -437,7 +445,7 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       }
     }
     sk = __fdiv_rn(key2f(kkey), T);
-    if (theta > neg_inf() && __fdiv_rn(below, T) >= sk) return false;
+    if ((use_below || theta > neg_inf()) && __fdiv_rn(below, T) >= sk) return false;
   }
   pc.mark(5);
   const float smax = __fdiv_rn(ymax, T);
@@ -681,6 +689,65 @@ __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm
   return -block_max<kSampleNT>(nlo, sm);
 }
 
+// Vocab-sharded mode, local half: the record of one row -- every local value
+// >= the local k-th value (ties kept; for greedy rows the local first maximum)
+// with global ids.  Rows that are neither greedy nor top-k <= kFastMaxK get
+// count -1.
+// `below`: an upper bound of the local values the source does not yield.
+template <class Src>
+__device__ void shard_emit(const Src& src, const tg_row_params& p, int V, int moff,
+                           tg_shard_record* rec, BlockScratch& sm, float below) {
+  const int t = threadIdx.x;
+  const bool greedy = !(p.temperature > 0.0f);
+  if (greedy) {
+    float y = neg_inf();
+    int id = 0x7fffffff;
+    src.for_each([&](int i, float v) {
+      if (v > y || (v == y && i < id)) { y = v; id = i; }
+    });
+    block_argmax<kSampleNT>(y, id, sm);
+    if (t == 0) {
+      rec->flags = 0;
+      rec->absent_max = neg_inf();
+      rec->count = id == 0x7fffffff ? 0 : 1;
+      if (id != 0x7fffffff) { rec->cand[0].value = y; rec->cand[0].id = id + moff; }
+    }
+    return;
+  }
+  if (!(p.top_k > 0 && p.top_k <= kFastMaxK)) {
+    if (t == 0) { rec->count = -1; rec->flags = 0; }
+    return;
+  }
+  float kth = neg_inf();
+  if (p.top_k < V) {
+    uint32_t kkey; unsigned long long b0, m0; unsigned int c0, n0;
+    const unsigned int k = static_cast<unsigned int>(p.top_k);
+    auto kw = [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; };
+    auto rc = [&](unsigned long long, unsigned int c) { return c >= k; };
+    radix_find<kSampleNT, true, false, Src, decltype(kw), decltype(rc), true>(src, 32, kw, rc, sm, kkey, b0, c0, n0, m0);
+    kth = key2f(kkey);
+  }
+  if (t == 0) sm.sn = 0;
+  __syncthreads();
+  float absent = below;
+  src.for_each([&](int i, float y) {
+    if (y >= kth && y > neg_inf()) {
+      const int pos = atomicAdd(&sm.sn, 1);
+      if (pos < TG_SHARD_CAP) { rec->cand[pos].value = y; rec->cand[pos].id = i + moff; }
+    } else {
+      absent = fmaxf(absent, y);
+    }
+  });
+  absent = block_max<kSampleNT>(absent, sm);
+  if (t == 0) {
+    const int c = sm.sn;
+    rec->count = c < TG_SHARD_CAP ? c : TG_SHARD_CAP;
+    rec->flags = c > TG_SHARD_CAP ? 1 : 0;
+    rec->absent_max = absent;
+  }
+  __syncthreads();
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(SampleArgs a) {
   using E = Elt<DT>;
@@ -691,6 +758,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   __shared__ uint32_t bloom[128];
   const int b = blockIdx.x;
   const int t = threadIdx.x;
+  const int moff = a.vocab_offset;  // global id of this shard's element 0
   const int V = a.vocab;
   float* cand_y = reinterpret_cast<float*>(dyn);
   int* cand_id = reinterpret_cast<int*>(dyn + kCandMax * 4);
@@ -710,8 +778,13 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
     const int sid = a.state_id[b];
     if (sid >= a.num_states) {
       if (t == 0) {
-        a.out_ids[b] = -1;
-        if (a.out_probs) a.out_probs[b] = 0.0f;
+        if (a.shard_out) {
+          a.shard_out[b].count = -1;
+          a.shard_out[b].flags = 0;
+        } else {
+          a.out_ids[b] = -1;
+          if (a.out_probs) a.out_probs[b] = 0.0f;
+        }
         atomicOr(a.status, 1u);
       }
       return;
@@ -762,7 +835,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
     __syncthreads();
     const int32_t* h = a.history + static_cast<int64_t>(b) * a.history_stride;
     for (int i = t; i < hlen; i += kSampleNT) {
-      const int id = h[i];
+      const int id = h[i] - moff;  // history ids are global
       if (id < 0 || id >= V) continue;
       int s = hist.slot0(id);
       for (;;) {
@@ -779,7 +852,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
       atomicOr(&bloom[hb >> 5], 1u << (hb & 31));
       if (!values) continue;
       float raw = E::load(row, id);
-      if (mask && !mask_allows(mask, id)) raw = neg_inf();
+      if (mask && !mask_allows(mask, moff + id)) raw = neg_inf();
       const float y = penalise(raw, hval[s]);
       hval[s] = __float_as_int(y);
       if (!(raw >= th) && y >= th) {
@@ -813,7 +886,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
       if (!mask) return E::vmax(w);
       float x[EPV];
       E::unpack(w, x);
-      const uint32_t bits = mask_bits(mask, head + j * EPV, EPV);
+      const uint32_t bits = mask_bits(mask, moff + head + j * EPV, EPV);
       float vm = neg_inf();
 #pragma unroll
       for (int e = 0; e < EPV; e++)
@@ -824,7 +897,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
     auto append_vec = [&](const uint4& w, int j, float th) {
       float x[EPV];
       E::unpack(w, x);
-      const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
+      const uint32_t bits = mask ? mask_bits(mask, moff + head + j * EPV, EPV) : 0xffu;
       uint32_t hits = 0;
 #pragma unroll
       for (int e = 0; e < EPV; e++) hits |= (((bits >> e) & 1u) && x[e] >= th ? 1u : 0u) << e;
@@ -844,7 +917,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
       else if (t - head < V - tail0) sc_id = tail0 + (t - head);
       if (sc_id < 0) return;
       float sc = E::load(row, sc_id);
-      if (mask && !mask_allows(mask, sc_id)) sc = neg_inf();
+      if (mask && !mask_allows(mask, moff + sc_id)) sc = neg_inf();
       if (sc >= th) {
         const int pos = atomicAdd(&sm.cand_count, 1);
         if (pos < kCandMax) { cand_y[pos] = sc; cand_id[pos] = sc_id; }
@@ -865,7 +938,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
         if (i < cnt) {
           j = ridx[i];
           E::unpack(rdata[i], x);
-          const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
+          const uint32_t bits = mask ? mask_bits(mask, moff + head + j * EPV, EPV) : 0xffu;
 #pragma unroll
           for (int e = 0; e < EPV; e++) hits |= (((bits >> e) & 1u) && x[e] >= th ? 1u : 0u) << e;
         }
@@ -981,7 +1054,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
             const int id = hkey[s];
             if (id < 0) continue;
             float raw = E::load(row, id);
-            if (mask && !mask_allows(mask, id)) raw = neg_inf();
+            if (mask && !mask_allows(mask, moff + id)) raw = neg_inf();
             const float py = __int_as_float(hval[s]);
             if (!(raw >= theta) && py >= theta) {
               const int pos = atomicAdd(&sm.cand_count, 1);
@@ -1004,6 +1077,10 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
       const unsigned int nvalid = block_count_if(src, theta, sm);
       if (t == 0) atomicAdd(&a.counters[5], static_cast<unsigned long long>(nvalid));
       pc.mark(4);
+      if (a.shard_out && !overflow && nvalid >= need) {  // vocab shard: emit the local record
+        shard_emit(src, p, V, moff, a.shard_out + b, sm, theta > neg_inf() ? key2f(fkey(theta) - 1u) : neg_inf());
+        return;
+      }
       if (!overflow && nvalid >= need) {
         const bool partial = !greedy && !topk && theta > neg_inf();
         unsigned long long qrest = 0;
@@ -1020,18 +1097,18 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
           };
           if (t < head) {
             float y = E::load(row, t);
-            if (mask && !mask_allows(mask, t)) y = neg_inf();
+            if (mask && !mask_allows(mask, moff + t)) y = neg_inf();
             qrest += rest(t, y);
           }
           if (t < V - tail0) {
             float y = E::load(row, tail0 + t);
-            if (mask && !mask_allows(mask, tail0 + t)) y = neg_inf();
+            if (mask && !mask_allows(mask, moff + tail0 + t)) y = neg_inf();
             qrest += rest(tail0 + t, y);
           }
           for (int j = t; j < nvec; j += kSampleNT) {
             float x[EPV];
             E::unpack(__ldg(vrow + j), x);
-            const uint32_t bits = mask ? mask_bits(mask, head + j * EPV, EPV) : 0xffu;
+            const uint32_t bits = mask ? mask_bits(mask, moff + head + j * EPV, EPV) : 0xffu;
 #pragma unroll
             for (int e = 0; e < EPV; e++) qrest += rest(head + j * EPV + e, ((bits >> e) & 1u) ? x[e] : neg_inf());
           }
@@ -1085,13 +1162,106 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
     if (t == 0) atomicAdd(&a.counters[4], 1ull);
     if (hist_counts_only) { hist.active = 0; __syncthreads(); }
     build_hist(__int_as_float(0x7f800000), true);
-    GlobalSrc<DT> src{row, V, head, nvec, tail0, mask, hist};
+    GlobalSrc<DT> src{row, V, head, nvec, tail0, mask, hist, moff};
+    if (a.shard_out) {
+      shard_emit(src, p, V, moff, a.shard_out + b, sm, neg_inf());
+      return;
+    }
     finish_row(src, p, V, u, false, neg_inf(), sm, out_id, out_prob);
     pc.mark(11);
   }
   if (t == 0) {
     a.out_ids[b] = out_id;
     if (a.out_probs) a.out_probs[b] = out_prob;
+  }
+}
+
+// ---- vocab-sharded mode, merge half ---------------------------------------
+struct MergeArgs {
+  const tg_shard_record* rec;  // [nshards][batch]
+  int32_t nshards;
+  int32_t batch;
+  int32_t full_vocab;
+  const tg_row_params* params;
+  const float* uniforms;
+  int32_t* out_ids;
+  float* out_probs;
+  uint32_t* status;
+};
+
+struct RecSrc {  // every entry of one row's records
+  const tg_shard_record* rec;
+  int nshards, batch, row;
+  template <class F>
+  __device__ __forceinline__ void for_each(F&& f) const {
+    for (int r = 0; r < nshards; r++) {
+      const tg_shard_record* x = rec + static_cast<int64_t>(r) * batch + row;
+      const int c = x->count;
+      for (int i = threadIdx.x; i < c; i += kSampleNT) f(x->cand[i].id, x->cand[i].value);
+    }
+  }
+};
+
+// One CTA per row.  The union of the shards' local top-k survivors holds every
+// element >= the global k-th value, so the global k-th is found over the union
+// and stages (b)-(e) run on the entries >= it, exactly as in sample_kernel.
+__global__ void __launch_bounds__(kSampleNT) sample_merge_kernel(MergeArgs m) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  __shared__ BlockScratch sm;
+  const int b = blockIdx.x;
+  const int t = threadIdx.x;
+  float* cand_y = reinterpret_cast<float*>(dyn);
+  int* cand_id = reinterpret_cast<int*>(dyn + kCandMax * 4);
+  float* cand_e = reinterpret_cast<float*>(dyn + kCandMax * 8);
+  const tg_row_params p = m.params[b];
+  const float u = m.uniforms ? m.uniforms[b] : 0.0f;
+  bool bad = false;
+  float absent = neg_inf();  // no value missing from the union exceeds this
+  for (int r = 0; r < m.nshards; r++) {
+    const tg_shard_record* x = m.rec + static_cast<int64_t>(r) * m.batch + b;
+    bad |= x->count < 0 || x->flags != 0;
+    absent = fmaxf(absent, x->absent_max);
+  }
+  int out_id = -1;
+  float out_prob = 0.0f;
+  RecSrc src{m.rec, m.nshards, m.batch, b};
+  if (!bad) {
+    const bool greedy = !(p.temperature > 0.0f);
+    float kth = neg_inf();
+    if (!greedy && p.top_k < m.full_vocab) {
+      uint32_t kkey; unsigned long long b0, m0; unsigned int c0, n0;
+      const unsigned int k = static_cast<unsigned int>(p.top_k);
+      auto kw = [&](int, float y, uint32_t& key, unsigned long long& w) {
+        if (!(y > neg_inf())) return false;
+        key = fkey(y); w = 0; return true;
+      };
+      auto rc = [&](unsigned long long, unsigned int c) { return c >= k; };
+      radix_find<kSampleNT, true, false, RecSrc, decltype(kw), decltype(rc), true>(src, 32, kw, rc, sm, kkey, b0, c0, n0, m0);
+      kth = key2f(kkey);
+    }
+    if (t == 0) sm.sn = 0;
+    __syncthreads();
+    src.for_each([&](int id, float y) {
+      if (y >= kth && y > neg_inf()) {
+        const int pos = atomicAdd(&sm.sn, 1);
+        if (pos < kCandMax) { cand_y[pos] = y; cand_id[pos] = id; }
+      }
+    });
+    __syncthreads();
+    const int n = sm.sn;
+    __syncthreads();
+    if (n > kCandMax) {
+      bad = true;
+    } else {
+      PhaseClock pc;
+      bad = !finish_cands(cand_y, cand_id, cand_e, n, kth, p, m.full_vocab, u, sm, out_id, out_prob, pc,
+                          false, 0ull, absent, true);
+    }
+  }
+  if (t == 0) {
+    if (bad) { out_id = -1; out_prob = 0.0f; atomicOr(m.status, 4u); }
+    m.out_ids[b] = out_id;
+    if (m.out_probs) m.out_probs[b] = out_prob;
   }
 }
 

@@ -162,7 +162,8 @@ int32_t tg_sampler_destroy(tg_sampler* s) {
   return TG_OK;
 }
 
-int32_t tg_sample(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_stride,
+static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_vocab,
+                             tg_shard_record* shard_out, const void* logits, int32_t dtype, int64_t row_stride,
                   int32_t batch, const tg_row_params* params, const int32_t* history,
                   const int32_t* history_len, int32_t history_stride,
                   const uint32_t* mask_table, int32_t num_states, const int32_t* state_id,
@@ -171,7 +172,7 @@ int32_t tg_sample(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_
   if (dtype != TG_DTYPE_F32 && dtype != TG_DTYPE_BF16) return fail(TG_ERR_INVALID_ARG, "dtype must be TG_DTYPE_F32 or TG_DTYPE_BF16");
   if (batch < 0 || batch > s->max_batch) return fail(TG_ERR_INVALID_ARG, "batch outside [0, max_batch]");
   if (batch == 0) return TG_OK;
-  if (!logits || !params || !out_ids) return fail(TG_ERR_INVALID_ARG, "logits, params and out_ids are required");
+  if (!logits || !params || (!out_ids && !shard_out)) return fail(TG_ERR_INVALID_ARG, "logits, params and out_ids are required");
   if (row_stride < s->vocab) return fail(TG_ERR_INVALID_ARG, "row_stride < vocab");
   const bool has_hist = history_len != nullptr;
   if (has_hist && (!history || history_stride <= 0)) return fail(TG_ERR_INVALID_ARG, "history_len given without history / history_stride");
@@ -196,7 +197,10 @@ int32_t tg_sample(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_
   }
   a.mask_table = has_mask ? mask_table : nullptr;
   a.num_states = has_mask ? num_states : 0;
-  a.mask_words = (s->vocab + 31) / 32;
+  a.mask_words = (full_vocab + 31) / 32;
+  a.vocab_offset = vocab_offset;
+  a.full_vocab = full_vocab;
+  a.shard_out = shard_out;
   a.state_id = has_mask ? state_id : nullptr;
   a.uniforms = uniforms;
   a.out_ids = out_ids;
@@ -210,6 +214,50 @@ int32_t tg_sample(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_
     tg::sample_kernel<0><<<batch, tg::kSampleNT, smem, st>>>(a);
   else
     tg::sample_kernel<1><<<batch, tg::kSampleNT, smem, st>>>(a);
+  TG_CUDA(cudaGetLastError());
+  return TG_OK;
+}
+
+int32_t tg_sample(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_stride,
+                  int32_t batch, const tg_row_params* params, const int32_t* history,
+                  const int32_t* history_len, int32_t history_stride,
+                  const uint32_t* mask_table, int32_t num_states, const int32_t* state_id,
+                  const float* uniforms, int32_t* out_ids, float* out_probs, void* stream) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  return launch_sample(s, 0, s->vocab, nullptr, logits, dtype, row_stride, batch, params, history,
+                       history_len, history_stride, mask_table, num_states, state_id, uniforms,
+                       out_ids, out_probs, stream);
+}
+
+int32_t tg_sample_shard_local(tg_sampler* s, int32_t vocab_offset, int32_t full_vocab,
+                              const void* logits, int32_t dtype, int64_t row_stride,
+                              int32_t batch, const tg_row_params* params,
+                              const int32_t* history, const int32_t* history_len,
+                              int32_t history_stride, const uint32_t* mask_table,
+                              int32_t num_states, const int32_t* state_id,
+                              tg_shard_record* out_records, void* stream) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (!out_records) return fail(TG_ERR_INVALID_ARG, "out_records is NULL");
+  if (vocab_offset < 0 || full_vocab > TG_MAX_VOCAB || static_cast<int64_t>(vocab_offset) + s->vocab > full_vocab)
+    return fail(TG_ERR_INVALID_ARG, "shard [vocab_offset, vocab_offset + vocab) outside [0, full_vocab <= TG_MAX_VOCAB)");
+  return launch_sample(s, vocab_offset, full_vocab, out_records, logits, dtype, row_stride, batch,
+                       params, history, history_len, history_stride, mask_table, num_states,
+                       state_id, nullptr, nullptr, nullptr, stream);
+}
+
+int32_t tg_sample_shard_merge(tg_sampler* s, const tg_shard_record* records, int32_t nshards,
+                              int32_t full_vocab, int32_t batch, const tg_row_params* params,
+                              const float* uniforms, int32_t* out_ids, float* out_probs,
+                              void* stream) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (batch < 0 || batch > s->max_batch) return fail(TG_ERR_INVALID_ARG, "batch outside [0, max_batch]");
+  if (nshards <= 0 || full_vocab <= 0 || full_vocab > TG_MAX_VOCAB) return fail(TG_ERR_INVALID_ARG, "bad nshards / full_vocab");
+  if (batch == 0) return TG_OK;
+  if (!records || !params || !out_ids) return fail(TG_ERR_INVALID_ARG, "records, params and out_ids are required");
+  DeviceGuard g(s->device);
+  tg::MergeArgs m{records, nshards, batch, full_vocab, params, uniforms, out_ids, out_probs, s->d_status};
+  tg::sample_merge_kernel<<<batch, tg::kSampleNT, static_cast<size_t>(tg::kCandMax) * 12,
+                            static_cast<cudaStream_t>(stream)>>>(m);
   TG_CUDA(cudaGetLastError());
   return TG_OK;
 }

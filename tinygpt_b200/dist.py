@@ -41,3 +41,23 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+def sample_vocab_sharded(sampler, logits_shard, params, vocab_offset: int, full_vocab: int, *,
+                         uniforms, history=None, history_len=None, mask_table=None,
+                         state_id=None, out_probs=None, group=None):
+    """Vocab-sharded sampling: this rank holds ids [vocab_offset, +shard width) of
+    every row.  Local records -> NCCL all-gather over NVLink -> identical merge on
+    every rank; returns the ids of the whole rows (what tg_sample returns on
+    them)."""
+    import torch
+    import torch.distributed as dist
+    rec = sampler.sample_shard_local(logits_shard, params, vocab_offset, full_vocab,
+                                     history=history, history_len=history_len,
+                                     mask_table=mask_table, state_id=state_id)
+    world = dist.get_world_size(group)
+    gathered = torch.empty((world,) + tuple(rec.shape), dtype=rec.dtype, device=rec.device)
+    dist.all_gather_into_tensor(gathered, rec, group=group)
+    ids, probs = sampler.sample_shard_merge(gathered, full_vocab, params, uniforms=uniforms,
+                                            out_probs=out_probs)
+    return ids, probs

@@ -166,6 +166,40 @@ class Sampler:
                                      _ptr(out_n), _stream_ptr(stream)))
         return out, out_n
 
+    def sample_shard_local(self, logits, params, vocab_offset: int, full_vocab: int, *,
+                           history=None, history_len=None, mask_table=None, state_id=None,
+                           out_records=None, stream=None):
+        """tg_sample_shard_local: this handle's vocab slice [vocab_offset, +vocab) of
+        every row -> one record per row (uint8 [B, SHARD_RECORD_BYTES])."""
+        B, stride = logits.shape
+        dev = logits.device
+        if isinstance(params, np.ndarray):
+            params = params_to_device(params, dev)
+        if out_records is None:
+            out_records = torch.empty((B, _lib.SHARD_RECORD_BYTES), dtype=torch.uint8, device=dev)
+        hstride = history.shape[1] if history is not None else 0
+        nstates = mask_table.shape[0] if mask_table is not None else 0
+        check(self._L.tg_sample_shard_local(self._h, vocab_offset, full_vocab, _ptr(logits),
+                                            _dtype_code(logits), logits.stride(0), B, _ptr(params),
+                                            _ptr(history), _ptr(history_len), hstride,
+                                            _ptr(mask_table), nstates, _ptr(state_id),
+                                            _ptr(out_records), _stream_ptr(stream)))
+        return out_records
+
+    def sample_shard_merge(self, records, full_vocab: int, params, *, uniforms=None, out=None,
+                           out_probs=None, stream=None):
+        """tg_sample_shard_merge over gathered records uint8 [nshards, B, RECORD]."""
+        nshards, B, _ = records.shape
+        dev = records.device
+        if isinstance(params, np.ndarray):
+            params = params_to_device(params, dev)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=dev)
+        check(self._L.tg_sample_shard_merge(self._h, _ptr(records), nshards, full_vocab, B,
+                                            _ptr(params), _ptr(uniforms), _ptr(out),
+                                            _ptr(out_probs), _stream_ptr(stream)))
+        return out, out_probs
+
     def path_counters(self, reset: bool = True) -> dict:
         """Row counts per sampling path since the last reset (see tgsample.h)."""
         buf = (ctypes.c_uint64 * 8)()
