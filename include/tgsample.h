@@ -221,7 +221,9 @@ int32_t tg_sample_shard_merge(tg_sampler* s, const tg_shard_record* records, int
  * the handle's device).  Bit 0: a state_id outside [0, num_states);
  * bit 1: a draft id outside [0, vocab); bit 2: a row the vocab-sharded mode
  * could not resolve (unsupported parameters, more than TG_SHARD_CAP local
- * survivors, or a top-k threshold tie between shards).  Cleared by this call. */
+ * survivors, or a top-k threshold tie between shards); bit 3: a bounded wait
+ * for a bulk copy into shared memory gave up (the affected statistics are
+ * unreliable).  Cleared by this call. */
 int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits);
 
 /* Per-handle path counters of tg_sample (diagnostics, the device-side analogue

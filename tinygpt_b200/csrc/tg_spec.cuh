@@ -3,22 +3,33 @@
 // Reference: native-mac/Sources/TinyGPT/SpeculativeDecode.swift:121-210
 // (stochastic, Leviathan et al.) and :41-98 (greedy).  The reference walks the
 // K positions on the host with two softmaxes and several device->host reads per
-// position; here two kernels do the whole batch:
-//   spec_stats_kernel  one CTA per (row, position, target|draft) vocab row:
-//                      max s = max x / T and the exact mass sum Z = sum q, plus
-//                      the first argmax (greedy rows).  One HBM pass for the
-//                      max, the second pass hits L2 (the row was just read).
-//   spec_verify_kernel one CTA per batch row: the sequential accept chain from
-//                      the stats, then the final draw (residual, target or bonus)
-//                      by an index-ordered chunked inverse CDF over the vocab.
+// position; here two cluster kernels do the whole batch:
+//   spec_stats_kernel   one 8-CTA cluster per (row, position, target|draft) vocab
+//                       row.  Each CTA stages its slice of the row in shared
+//                       memory with one 1-D TMA bulk copy (cp.async.bulk, no
+//                       multicast), the row maximum and the exact mass sum
+//                       Z = sum q are combined over distributed shared memory:
+//                       the row is read from HBM once.
+//   spec_verify_kernel  one 8-CTA cluster per batch row.  Rank 0 runs the
+//                       sequential accept chain; every CTA sums the final
+//                       distribution's masses over its slice; the slice sums,
+//                       exchanged over DSMEM, locate the slice holding the draw
+//                       point, whose CTA finds the id with an ordered scan.
 #pragma once
+
+#include <cooperative_groups.h>
 
 #include "../../include/tgsample.h"
 #include "tg_block.cuh"
 
 namespace tg {
 
-constexpr int kSpecNT = 512;
+namespace cg = cooperative_groups;
+
+constexpr int kSpecNT = 256;
+constexpr int kSpecCluster = 8;
+constexpr int kSpecMaxStage = 200 * 1024;     // bytes of a staged slice
+constexpr unsigned kWaitLimit = 1u << 22;     // bounded mbarrier waits
 
 struct __align__(16) SpecStat {
   float smax;
@@ -40,82 +51,138 @@ struct SpecArgs {
   int32_t* out_n;
   SpecStat* stats;  // [batch, 2K+1]
   uint32_t* status;
+  int32_t chunk;    // elements per cluster rank (multiple of 8)
 };
 
 __device__ __forceinline__ float spec_T(float t0) { return fmaxf(t0, 1e-5f); }
 
-// Visit every element of a vocab row: 128-bit loads over the aligned middle,
-// scalar loads for the unaligned head and tail.  f(v, x) per element.
-template <int DT, int NT, class F>
-__device__ __forceinline__ void row_for_each(const void* rowv, int V, F&& f) {
-  using E = Elt<DT>;
-  constexpr int EPV = E::kEPV;
-  const char* row = reinterpret_cast<const char*>(rowv);
-  const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
-  int head = static_cast<int>(((16u - (addr & 15u)) & 15u) / E::kSize);
-  if (head > V) head = V;
-  const int nvec = (V - head) / EPV;
-  const int tail0 = head + nvec * EPV;
-  const uint4* vrow = reinterpret_cast<const uint4*>(row + head * E::kSize);
-  const int t = threadIdx.x;
-  if (t < head) f(t, E::load(row, t));
-  if (t < V - tail0) f(tail0 + t, E::load(row, tail0 + t));
-  for (int jb = 0; jb < nvec; jb += 4 * NT) {
-    uint4 w[4];
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int j = jb + q * NT + t;
-      if (j < nvec) w[q] = ldg_stream(vrow + j);
-    }
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int j = jb + q * NT + t;
-      if (j < nvec) {
-        float x[EPV];
-        E::unpack(w[q], x);
-#pragma unroll
-        for (int e = 0; e < EPV; e++) f(head + j * EPV + e, x[e]);
-      }
-    }
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Bounded wait on phase 0 of an mbarrier; false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar) {
+  for (unsigned it = 0; it < kWaitLimit; it++) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_u32(bar))
+        : "memory");
+    if (done) return true;
   }
+  return false;
+}
+
+// Stage elements [c0, c1) of `row` into shared memory `dst` (raw dtype): the
+// 16-byte-aligned body by one bulk copy completing on `bar`, the rest by plain
+// loads.  Returns whether a bulk copy was issued (then wait on bar).
+template <int DT>
+__device__ __forceinline__ bool stage_slice(const char* row, int c0, int c1, unsigned char* dst,
+                                            uint64_t* bar) {
+  using E = Elt<DT>;
+  const int n = c1 - c0;
+  const char* src = row + static_cast<int64_t>(c0) * E::kSize;
+  const bool aligned = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+  const int nb = aligned ? ((n * E::kSize) & ~15) : 0;
+  if (threadIdx.x == 0 && nb > 0) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(nb)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(nb), "r"(smem_u32(bar))
+        : "memory");
+  }
+  for (int i = nb / E::kSize + threadIdx.x; i < n; i += kSpecNT) {
+    if (E::kSize == 4) reinterpret_cast<float*>(dst)[i] = E::load(src, i);
+    else reinterpret_cast<uint16_t*>(dst)[i] = reinterpret_cast<const uint16_t*>(src)[i];
+  }
+  return nb > 0;
 }
 
 template <int DT>
-__global__ void __launch_bounds__(kSpecNT) spec_stats_kernel(SpecArgs a) {
+__device__ __forceinline__ float smem_elem(const unsigned char* buf, int i) {
+  if (Elt<DT>::kSize == 4) return reinterpret_cast<const float*>(buf)[i];
+  return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(buf)[i]) << 16);
+}
+
+template <int DT>
+__global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
+    spec_stats_kernel(SpecArgs a) {
+  using E = Elt<DT>;
+  extern __shared__ __align__(128) unsigned char slice[];
+  __shared__ __align__(8) uint64_t bar;
   __shared__ BlockScratch sm;
+  __shared__ float c_max;
+  __shared__ int c_arg;
+  __shared__ unsigned long long c_z;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int t = threadIdx.x;
   const int P = 2 * a.K + 1;
-  const int r = blockIdx.x;
+  const int r = blockIdx.x / kSpecCluster;
   const int b = r / P, pos = r % P;
   const int V = a.vocab;
   const float t0 = a.temperature[b];
   const bool greedy = !(t0 > 0.0f);
-  const void* row;
+  if (pos > a.K && greedy) return;  // the whole cluster: the draft row is not needed
+  const char* row;
   if (pos <= a.K) {
-    row = reinterpret_cast<const char*>(a.target) +
-          (static_cast<int64_t>(b) * (a.K + 1) + pos) * V * Elt<DT>::kSize;
+    row = reinterpret_cast<const char*>(a.target) + (static_cast<int64_t>(b) * (a.K + 1) + pos) * V * E::kSize;
   } else {
-    if (greedy) return;
-    row = reinterpret_cast<const char*>(a.draft) +
-          (static_cast<int64_t>(b) * a.K + (pos - a.K - 1)) * V * Elt<DT>::kSize;
+    row = reinterpret_cast<const char*>(a.draft) + (static_cast<int64_t>(b) * a.K + (pos - a.K - 1)) * V * E::kSize;
   }
+  const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
+  if (t == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const bool bulk = stage_slice<DT>(row, c0, c1, slice, &bar);
+  bool ok = true;
+  if (bulk) ok = mbar_wait(&bar);
+  __syncthreads();
+  // pass 1: maximum and its first index
   float y = neg_inf();
   int id = 0x7fffffff;
-  row_for_each<DT, kSpecNT>(row, V, [&](int v, float x) {
-    if (x > y || (x == y && v < id)) { y = x; id = v; }
-  });
+  if (ok) {
+    for (int i = t; i < c1 - c0; i += kSpecNT) {
+      const float x = smem_elem<DT>(slice, i);
+      if (x > y) { y = x; id = c0 + i; }
+    }
+  }
   block_argmax<kSpecNT>(y, id, sm);
+  if (t == 0) { c_max = y; c_arg = id; }
+  cluster.sync();
+  for (int q = 0; q < kSpecCluster; q++) {
+    const float oy = *cluster.map_shared_rank(&c_max, q);
+    const int oi = *cluster.map_shared_rank(&c_arg, q);
+    if (q == 0 || oy > y || (oy == y && oi < id)) { y = oy; id = oi; }
+  }
   if (greedy) {
-    if (threadIdx.x == 0) a.stats[r] = SpecStat{y, id, 0ull};
+    if (rank == 0 && t == 0) a.stats[r] = SpecStat{y, id, 0ull};
+    cluster.sync();  // peers still read this CTA's maximum
     return;
   }
   const float T = spec_T(t0);
   const float smax = __fdiv_rn(y, T);
   unsigned long long Z = 0;
-  row_for_each<DT, kSpecNT>(row, V, [&](int, float x) {
-    Z += qmass(__fsub_rn(__fdiv_rn(x, T), smax));
-  });
+  if (ok) {
+    for (int i = t; i < c1 - c0; i += kSpecNT)
+      Z += qmass(__fsub_rn(__fdiv_rn(smem_elem<DT>(slice, i), T), smax));
+  }
   Z = block_sum<kSpecNT>(Z, sm);
-  if (threadIdx.x == 0) a.stats[r] = SpecStat{smax, id, Z};
+  if (t == 0) c_z = Z;
+  cluster.sync();
+  if (rank == 0 && t == 0) {
+    unsigned long long tot = 0;
+    for (int q = 0; q < kSpecCluster; q++) tot += *cluster.map_shared_rank(&c_z, q);
+    a.stats[r] = SpecStat{smax, id, tot};
+  }
+  if (!ok && t == 0) atomicOr(a.status, 8u);
+  cluster.sync();
+  if (!ok && bulk) mbar_wait(&bar);  // never leave with the copy in flight if it can be helped
 }
 
 // Residual mass of one token: trunc(max(0, qT/ZT - qD/ZD) * 2^52).
@@ -126,12 +193,16 @@ __device__ __forceinline__ unsigned long long resid_mass(unsigned long long qT, 
 }
 
 template <int DT>
-__global__ void __launch_bounds__(kSpecNT) spec_verify_kernel(SpecArgs a) {
+__global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
+    spec_verify_kernel(SpecArgs a) {
   using E = Elt<DT>;
   __shared__ BlockScratch sm;
-  __shared__ int s_final;  // -1: all accepted (bonus), else the rejecting position
-  __shared__ int s_n;
-  const int b = blockIdx.x;
+  __shared__ int s_fin, s_n;  // rank 0: the rejecting position (-1 bonus, -2 done) and accepted count
+  __shared__ unsigned long long c_sumT, c_sumR;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int t = threadIdx.x;
+  const int b = blockIdx.x / kSpecCluster;
   const int K = a.K, V = a.vocab, P = 2 * K + 1;
   const float t0 = a.temperature[b];
   const bool greedy = !(t0 > 0.0f);
@@ -141,7 +212,7 @@ __global__ void __launch_bounds__(kSpecNT) spec_verify_kernel(SpecArgs a) {
   const char* tgt = reinterpret_cast<const char*>(a.target) + static_cast<int64_t>(b) * (K + 1) * V * E::kSize;
   const char* drf = greedy ? nullptr : reinterpret_cast<const char*>(a.draft) + static_cast<int64_t>(b) * K * V * E::kSize;
 
-  if (threadIdx.x == 0) {
+  if (rank == 0 && t == 0) {
     for (int i = 0; i <= K; i++) out[i] = -1;
     int n = 0, fin = -1;
     for (int i = 0; i < K; i++) {
@@ -150,7 +221,7 @@ __global__ void __launch_bounds__(kSpecNT) spec_verify_kernel(SpecArgs a) {
         const int am = st[i].argmax;
         if (am == tok) { out[n++] = tok; continue; }
         out[n++] = am;
-        fin = -2;  // done, nothing to draw
+        fin = -2;
         break;
       }
       bool accept = false;
@@ -173,18 +244,20 @@ __global__ void __launch_bounds__(kSpecNT) spec_verify_kernel(SpecArgs a) {
       out[n++] = st[K].argmax;
       fin = -2;
     }
-    s_final = fin;
+    s_fin = fin;
     s_n = n;
   }
-  __syncthreads();
-  const int fin = s_final;
+  cluster.sync();
+  const int fin = *cluster.map_shared_rank(&s_fin, 0);
+  const int n0 = *cluster.map_shared_rank(&s_n, 0);
   if (fin == -2) {
-    if (threadIdx.x == 0) a.out_n[b] = s_n;
+    if (rank == 0 && t == 0) a.out_n[b] = n0;
+    cluster.sync();
     return;
   }
 
-  // Final draw over the vocab in index order.  Thread t owns the contiguous
-  // chunk [t*C, t*C+C); chunk sums -> block scan -> the owning thread rescans.
+  // Final draw over the vocab in index order: this CTA's slice [c0, c1),
+  // thread t owning the contiguous part [c0 + t*sub, ...).
   const int pos = fin < 0 ? K : fin;
   const char* trow = tgt + static_cast<int64_t>(pos) * V * E::kSize;
   const char* drow = fin < 0 ? nullptr : drf + static_cast<int64_t>(fin) * V * E::kSize;
@@ -192,38 +265,74 @@ __global__ void __launch_bounds__(kSpecNT) spec_verify_kernel(SpecArgs a) {
   const double ZT = __ull2double_rn(st[pos].Z);
   const float smD = fin < 0 ? 0.0f : st[K + 1 + fin].smax;
   const double ZD = fin < 0 ? 1.0 : __ull2double_rn(st[K + 1 + fin].Z);
-  const int C = (V + kSpecNT - 1) / kSpecNT;
-  const int v0 = threadIdx.x * C;
-  const int v1 = min(V, v0 + C);
+  const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
+  const int sub = (c1 - c0 + kSpecNT - 1) / kSpecNT;
+  const int v0 = min(c1, c0 + t * sub), v1 = min(c1, v0 + sub);
   auto qt_of = [&](int v) { return qmass(__fsub_rn(__fdiv_rn(E::load(trow, v), T), smT)); };
   auto rq_of = [&](int v) {
     const unsigned long long qd = qmass(__fsub_rn(__fdiv_rn(E::load(drow, v), T), smD));
     return resid_mass(qt_of(v), ZT, qd, ZD);
   };
-  bool use_resid = false;
-  unsigned long long csum = 0, total = 0;
+  unsigned long long sT = 0, sR = 0;
   if (fin >= 0) {
-    for (int v = v0; v < v1; v++) csum += rq_of(v);
-    unsigned long long R;
-    block_excl_scan<kSpecNT>(csum, R, sm);
-    use_resid = __dmul_rn(__ull2double_rn(R), 1.0 / kResidScale) > 1e-10;
+    for (int v = v0; v < v1; v++) {
+      const unsigned long long qt = qt_of(v);
+      const unsigned long long qd = qmass(__fsub_rn(__fdiv_rn(E::load(drow, v), T), smD));
+      sT += qt;
+      sR += resid_mass(qt, ZT, qd, ZD);
+    }
+  } else {
+    for (int v = v0; v < v1; v++) sT += qt_of(v);
   }
-  if (!use_resid) {
-    csum = 0;
-    for (int v = v0; v < v1; v++) csum += qt_of(v);
+  unsigned long long ctaT, ctaR;
+  const unsigned long long befT = block_excl_scan<kSpecNT>(sT, ctaT, sm);
+  const unsigned long long befR = block_excl_scan<kSpecNT>(sR, ctaR, sm);
+  if (t == 0) { c_sumT = ctaT; c_sumR = ctaR; }
+  cluster.sync();
+  unsigned long long totT = 0, totR = 0, preT = 0, preR = 0;
+  for (int q = 0; q < kSpecCluster; q++) {
+    const unsigned long long xT = *cluster.map_shared_rank(&c_sumT, q);
+    const unsigned long long xR = *cluster.map_shared_rank(&c_sumR, q);
+    if (q < rank) { preT += xT; preR += xR; }
+    totT += xT;
+    totR += xR;
   }
-  const unsigned long long before = block_excl_scan<kSpecNT>(csum, total, sm);
-  const unsigned long long r = draw_point(a.u_draw[b], total);
-  if (csum > 0 && before <= r && r < before + csum) {
+  const bool use_resid = fin >= 0 && __dmul_rn(__ull2double_rn(totR), 1.0 / kResidScale) > 1e-10;
+  const unsigned long long total = use_resid ? totR : totT;
+  const unsigned long long mine = use_resid ? sR : sT;
+  const unsigned long long before = (use_resid ? preR + befR : preT + befT);
+  const unsigned long long rpt = draw_point(a.u_draw[b], total);
+  if (mine > 0 && before <= rpt && rpt < before + mine) {
     unsigned long long c = before;
     int pick = v1 - 1;
     for (int v = v0; v < v1; v++) {
       c += use_resid ? rq_of(v) : qt_of(v);
-      if (c > r) { pick = v; break; }
+      if (c > rpt) { pick = v; break; }
     }
-    out[s_n] = pick;
-    a.out_n[b] = s_n + 1;
+    out[n0] = pick;
+    a.out_n[b] = n0 + 1;
   }
+  cluster.sync();  // keep this CTA's shared memory alive for its peers
+}
+
+// Both kernels of one verification on `st`.
+template <int DT>
+inline cudaError_t launch_spec(SpecArgs a, cudaStream_t st) {
+  const int esz = Elt<DT>::kSize;
+  int chunk = (a.vocab + kSpecCluster - 1) / kSpecCluster;
+  chunk = (chunk + 7) / 8 * 8;
+  a.chunk = chunk;
+  const size_t stage = static_cast<size_t>(chunk) * esz;
+  if (stage > static_cast<size_t>(kSpecMaxStage)) return cudaErrorInvalidValue;
+  if (stage > 48 * 1024) {  // per device; cheap enough to repeat
+    cudaError_t e = cudaFuncSetAttribute(spec_stats_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSpecMaxStage);
+    if (e != cudaSuccess) return e;
+  }
+  const int nrows = a.batch * (2 * a.K + 1);
+  spec_stats_kernel<DT><<<nrows * kSpecCluster, kSpecNT, stage, st>>>(a);
+  spec_verify_kernel<DT><<<a.batch * kSpecCluster, kSpecNT, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 }  // namespace tg

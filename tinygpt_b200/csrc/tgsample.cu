@@ -351,15 +351,9 @@ int32_t tg_spec_verify(tg_sampler* s, const void* target_logits, const void* dra
                  u_accept, u_draw, out_ids, out_n, static_cast<tg::SpecStat*>(s->stats.p),
                  s->d_status};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int nrows = batch * (2 * K + 1);
-  if (dtype == TG_DTYPE_F32) {
-    tg::spec_stats_kernel<0><<<nrows, tg::kSpecNT, 0, st>>>(a);
-    tg::spec_verify_kernel<0><<<batch, tg::kSpecNT, 0, st>>>(a);
-  } else {
-    tg::spec_stats_kernel<1><<<nrows, tg::kSpecNT, 0, st>>>(a);
-    tg::spec_verify_kernel<1><<<batch, tg::kSpecNT, 0, st>>>(a);
-  }
-  TG_CUDA(cudaGetLastError());
+  const cudaError_t le = dtype == TG_DTYPE_F32 ? tg::launch_spec<0>(a, st) : tg::launch_spec<1>(a, st);
+  if (le == cudaErrorInvalidValue) return fail(TG_ERR_UNSUPPORTED, "vocab too large for the staged verification (vocab * element size > 1.6 MB)");
+  TG_CUDA(le);
   return TG_OK;
 }
 
@@ -389,15 +383,9 @@ int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_
   TG_CUDA(cudaMemsetAsync(status, 0, sizeof(uint32_t), st));
   tg::SpecArgs a{target_logits, draft_logits, batch, K, vocab, draft_ids, temperature,
                  u_accept, u_draw, out_ids, out_n, stats, status};
-  const int nrows = batch * (2 * K + 1);
-  if (dtype == TG_DTYPE_F32) {
-    tg::spec_stats_kernel<0><<<nrows, tg::kSpecNT, 0, st>>>(a);
-    tg::spec_verify_kernel<0><<<batch, tg::kSpecNT, 0, st>>>(a);
-  } else {
-    tg::spec_stats_kernel<1><<<nrows, tg::kSpecNT, 0, st>>>(a);
-    tg::spec_verify_kernel<1><<<batch, tg::kSpecNT, 0, st>>>(a);
-  }
-  TG_CUDA(cudaGetLastError());
+  const cudaError_t le = dtype == TG_DTYPE_F32 ? tg::launch_spec<0>(a, st) : tg::launch_spec<1>(a, st);
+  if (le == cudaErrorInvalidValue) return fail(TG_ERR_UNSUPPORTED, "vocab too large for the staged verification (vocab * element size > 1.6 MB)");
+  TG_CUDA(le);
   return TG_OK;
 }
 
