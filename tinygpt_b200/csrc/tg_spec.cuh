@@ -52,6 +52,11 @@ struct SpecArgs {
   SpecStat* stats;  // [batch, 2K+1]
   uint32_t* status;
   int32_t chunk;    // elements per cluster rank (multiple of 8)
+  // lazy mode: positions are evaluated one at a time for the rows still
+  // accepting; rstate[2b] = accepted count, rstate[2b+1] = -1 while accepting,
+  // the rejecting position, or -2 when the row is finished (greedy)
+  int32_t* rstate;  // nullptr: eager (every position at once)
+  int32_t lazy_pos; // position of this lazy stats launch (K: the bonus row)
 };
 
 __device__ __forceinline__ float spec_T(float t0) { return fmaxf(t0, 1e-5f); }
@@ -121,8 +126,21 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const int rank = static_cast<int>(cluster.block_rank());
   const int t = threadIdx.x;
   const int P = 2 * a.K + 1;
-  const int r = blockIdx.x / kSpecCluster;
-  const int b = r / P, pos = r % P;
+  int b, pos;
+  if (!a.rstate) {  // eager: every (row, position) at once
+    b = (blockIdx.x / kSpecCluster) / P;
+    pos = (blockIdx.x / kSpecCluster) % P;
+  } else if (a.lazy_pos < a.K) {  // lazy: target and draft rows of one position
+    const int rl = blockIdx.x / kSpecCluster;
+    b = rl >> 1;
+    pos = (rl & 1) ? a.K + 1 + a.lazy_pos : a.lazy_pos;
+    if (a.lazy_pos > 0 && a.rstate[2 * b + 1] != -1) return;  // the whole cluster
+  } else {  // lazy: the bonus row of the rows that accepted every proposal
+    b = blockIdx.x / kSpecCluster;
+    pos = a.K;
+    if (a.K > 0 && a.rstate[2 * b + 1] != -1) return;
+  }
+  const int r = b * P + pos;
   const int V = a.vocab;
   const float t0 = a.temperature[b];
   const bool greedy = !(t0 > 0.0f);
@@ -192,6 +210,61 @@ __device__ __forceinline__ unsigned long long resid_mass(unsigned long long qT, 
   return d > 0.0 ? __double2ull_rz(__dmul_rn(d, kResidScale)) : 0ull;
 }
 
+// One accept test of batch row b at position i (thread-level): appends to out
+// and sets fin to i on a stochastic reject, -2 on a greedy mismatch.
+template <int DT>
+__device__ __forceinline__ void spec_accept_step(const SpecArgs& a, int b, int i, int32_t* out,
+                                                 int& n, int& fin) {
+  using E = Elt<DT>;
+  const int K = a.K, V = a.vocab, P = 2 * K + 1;
+  const float t0 = a.temperature[b];
+  const bool greedy = !(t0 > 0.0f);
+  const float T = spec_T(t0);
+  const SpecStat* st = a.stats + static_cast<int64_t>(b) * P;
+  const int tok = a.draft_ids[static_cast<int64_t>(b) * K + i];
+  if (greedy) {
+    const int am = st[i].argmax;
+    out[n++] = am;
+    if (am != tok) fin = -2;
+    return;
+  }
+  bool accept = false;
+  if (tok >= 0 && tok < V) {
+    const char* trow = reinterpret_cast<const char*>(a.target) + (static_cast<int64_t>(b) * (K + 1) + i) * V * E::kSize;
+    const char* drow = reinterpret_cast<const char*>(a.draft) + (static_cast<int64_t>(b) * K + i) * V * E::kSize;
+    const unsigned long long qT = qmass(__fsub_rn(__fdiv_rn(E::load(trow, tok), T), st[i].smax));
+    const unsigned long long qD = qmass(__fsub_rn(__fdiv_rn(E::load(drow, tok), T), st[K + 1 + i].smax));
+    const double pT = __ddiv_rn(__ull2double_rn(qT), __ull2double_rn(st[i].Z));
+    const double pD = __ddiv_rn(__ull2double_rn(qD), __ull2double_rn(st[K + 1 + i].Z));
+    const double ratio = __ddiv_rn(pT, pD > 1e-10 ? pD : 1e-10);
+    const double lim = ratio < 1.0 ? ratio : 1.0;
+    accept = static_cast<double>(a.u_accept[static_cast<int64_t>(b) * K + i]) <= lim;
+  } else {
+    atomicOr(a.status, 2u);
+  }
+  if (accept) out[n++] = tok;
+  else fin = i;
+}
+
+// Lazy mode: position i of every row still accepting, one thread per row.
+template <int DT>
+__global__ void __launch_bounds__(128) spec_chain_kernel(SpecArgs a, int i) {
+  const int b = blockIdx.x * 128 + threadIdx.x;
+  if (b >= a.batch) return;
+  int32_t* out = a.out_ids + static_cast<int64_t>(b) * (a.K + 1);
+  int n = 0, fin = -1;
+  if (i == 0) {
+    for (int j = 0; j <= a.K; j++) out[j] = -1;
+  } else {
+    n = a.rstate[2 * b];
+    fin = a.rstate[2 * b + 1];
+    if (fin != -1) return;
+  }
+  spec_accept_step<DT>(a, b, i, out, n, fin);
+  a.rstate[2 * b] = n;
+  a.rstate[2 * b + 1] = fin;
+}
+
 template <int DT>
 __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     spec_verify_kernel(SpecArgs a) {
@@ -213,34 +286,17 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const char* drf = greedy ? nullptr : reinterpret_cast<const char*>(a.draft) + static_cast<int64_t>(b) * K * V * E::kSize;
 
   if (rank == 0 && t == 0) {
-    for (int i = 0; i <= K; i++) out[i] = -1;
     int n = 0, fin = -1;
-    for (int i = 0; i < K; i++) {
-      const int tok = a.draft_ids[static_cast<int64_t>(b) * K + i];
-      if (greedy) {
-        const int am = st[i].argmax;
-        if (am == tok) { out[n++] = tok; continue; }
-        out[n++] = am;
-        fin = -2;
-        break;
-      }
-      bool accept = false;
-      if (tok >= 0 && tok < V) {
-        const unsigned long long qT = qmass(__fsub_rn(__fdiv_rn(E::load(tgt + static_cast<int64_t>(i) * V * E::kSize, tok), T), st[i].smax));
-        const unsigned long long qD = qmass(__fsub_rn(__fdiv_rn(E::load(drf + static_cast<int64_t>(i) * V * E::kSize, tok), T), st[K + 1 + i].smax));
-        const double pT = __ddiv_rn(__ull2double_rn(qT), __ull2double_rn(st[i].Z));
-        const double pD = __ddiv_rn(__ull2double_rn(qD), __ull2double_rn(st[K + 1 + i].Z));
-        const double ratio = __ddiv_rn(pT, pD > 1e-10 ? pD : 1e-10);
-        const double lim = ratio < 1.0 ? ratio : 1.0;
-        accept = static_cast<double>(a.u_accept[static_cast<int64_t>(b) * K + i]) <= lim;
-      } else {
-        atomicOr(a.status, 2u);
-      }
-      if (accept) { out[n++] = tok; continue; }
-      fin = i;
-      break;
+    if (!a.rstate) {
+      for (int i = 0; i <= K; i++) out[i] = -1;
+      for (int i = 0; i < K && fin == -1; i++) spec_accept_step<DT>(a, b, i, out, n, fin);
+    } else if (K == 0) {
+      out[0] = -1;
+    } else {
+      n = a.rstate[2 * b];
+      fin = a.rstate[2 * b + 1];
     }
-    if (greedy && fin == -1) {
+    if (greedy && fin == -1) {  // every proposal matched: the bonus is the target argmax
       out[n++] = st[K].argmax;
       fin = -2;
     }
@@ -315,7 +371,11 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   cluster.sync();  // keep this CTA's shared memory alive for its peers
 }
 
-// Both kernels of one verification on `st`.
+// One verification on `st`.  Eager: statistics of every position, then the
+// chain and the draw (two launches).  Lazy (rstate given): statistics of
+// position i only for the rows still accepting, i = 0..K-1, each followed by
+// the accept test, then the bonus row of the rows that accepted everything,
+// then the draw (2K + 2 launches, fewer vocab rows read).
 template <int DT>
 inline cudaError_t launch_spec(SpecArgs a, cudaStream_t st) {
   const int esz = Elt<DT>::kSize;
@@ -329,8 +389,18 @@ inline cudaError_t launch_spec(SpecArgs a, cudaStream_t st) {
                                          kSpecMaxStage);
     if (e != cudaSuccess) return e;
   }
-  const int nrows = a.batch * (2 * a.K + 1);
-  spec_stats_kernel<DT><<<nrows * kSpecCluster, kSpecNT, stage, st>>>(a);
+  if (!a.rstate) {
+    const int nrows = a.batch * (2 * a.K + 1);
+    spec_stats_kernel<DT><<<nrows * kSpecCluster, kSpecNT, stage, st>>>(a);
+  } else {
+    for (int i = 0; i < a.K; i++) {
+      a.lazy_pos = i;
+      spec_stats_kernel<DT><<<a.batch * 2 * kSpecCluster, kSpecNT, stage, st>>>(a);
+      spec_chain_kernel<DT><<<(a.batch + 127) / 128, 128, 0, st>>>(a, i);
+    }
+    a.lazy_pos = a.K;
+    spec_stats_kernel<DT><<<a.batch * kSpecCluster, kSpecNT, stage, st>>>(a);
+  }
   spec_verify_kernel<DT><<<a.batch * kSpecCluster, kSpecNT, 0, st>>>(a);
   return cudaGetLastError();
 }

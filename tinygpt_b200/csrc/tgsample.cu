@@ -102,7 +102,7 @@ struct tg_sampler {
   int max_batch = 0;
   uint32_t* d_status = nullptr;  // device error word
   unsigned long long* d_counters = nullptr;  // TG_PATH_* counters
-  DevBuf stats;                  // spec-verify statistics
+  DevBuf stats;                  // spec-verify statistics (+ per-row state of the lazy mode)
   // staging for tg_sample_host
   DevBuf h_logits, h_params, h_hist, h_hlen, h_mask, h_state, h_unif, h_out, h_prob;
   cudaStream_t stream = nullptr;  // used by tg_sample_host only
@@ -346,10 +346,11 @@ int32_t tg_spec_verify(tg_sampler* s, const void* target_logits, const void* dra
   std::lock_guard<std::mutex> lk(s->mu);
   DeviceGuard g(s->device);
   const size_t nst = sizeof(tg::SpecStat) * static_cast<size_t>(batch) * (2 * K + 1);
-  TG_CUDA(s->stats.ensure(nst));
+  TG_CUDA(s->stats.ensure(nst + sizeof(int32_t) * 2 * static_cast<size_t>(batch)));
   tg::SpecArgs a{target_logits, draft_logits, batch, K, s->vocab, draft_ids, temperature,
                  u_accept, u_draw, out_ids, out_n, static_cast<tg::SpecStat*>(s->stats.p),
                  s->d_status};
+  a.rstate = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(s->stats.p) + nst);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaError_t le = dtype == TG_DTYPE_F32 ? tg::launch_spec<0>(a, st) : tg::launch_spec<1>(a, st);
   if (le == cudaErrorInvalidValue) return fail(TG_ERR_UNSUPPORTED, "vocab too large for the staged verification (vocab * element size > 1.6 MB)");
