@@ -239,6 +239,58 @@ int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits);
 #define TG_PATH_COUNTERS 8
 int32_t tg_sampler_path_counters(tg_sampler* s, uint64_t* out, int32_t n, int32_t reset);
 
+/* ---------------------------------------------------------------------------
+ * Grammar compiler (host only; no GPU needed): grammar text -> byte-level
+ * automaton -> per-state token bitmasks, the rows of tg_sample's mask_table.
+ * Replaces the reference's constrained-decoding stack:
+ *   ServeGrammarSpec.parse / ServeConstraint / ServeTokenMasker
+ *     (native-mac/Sources/TinyGPTServe/Serve.swift:1903-2056),
+ *   JSONSchemaNode (native-mac/Sources/TinyGPTModel/JSONSchema.swift:1-117),
+ *   JSONSchemaFSM / LogitsMasker (native-mac/Sources/TinyGPTModel/ConstrainedGen.swift:35-837),
+ *   PaceToolTagFSM (Serve.swift:2057-2233, grammars/pace-tool-tags.gbnf).
+ * Grammar text: after trimming whitespace, text starting with '{' is a JSON
+ * Schema (minified JSON only; object keys limited to the declared properties
+ * not yet emitted; required keys before '}'; string enum / minLength /
+ * maxLength; integer vs number; no trailing commas); a GBNF text holding
+ * `root ::=` and `[POINT:` is the tool-tag grammar; anything else is
+ * TG_ERR_UNSUPPORTED.
+ *
+ * Vocabulary: token i is bytes token_bytes[token_offsets[i] .. token_offsets[i+1]).
+ * A token is allowed iff the automaton accepts all of its bytes; empty tokens
+ * never are.  Once the document is complete only eos_id is allowed (none if
+ * eos_id is -1, as in the serve masker). */
+#define TG_GRAMMAR_JSON_SCHEMA 0
+#define TG_GRAMMAR_TOOL_TAGS 1
+typedef struct tg_grammar tg_grammar;
+typedef struct tg_grammar_state tg_grammar_state;
+
+const char* tg_grammar_last_error(void);
+int32_t tg_grammar_create(const char* grammar_text, int64_t text_len, int32_t vocab,
+                          const uint8_t* token_bytes, const int64_t* token_offsets,
+                          int32_t eos_id, tg_grammar** out);
+int32_t tg_grammar_destroy(tg_grammar* g);
+int32_t tg_grammar_kind(tg_grammar* g, int32_t* kind);
+/* A fresh automaton at the document start (one per generated sequence). */
+int32_t tg_grammar_state_create(tg_grammar* g, tg_grammar_state** out);
+int32_t tg_grammar_state_clone(const tg_grammar_state* s, tg_grammar_state** out);
+int32_t tg_grammar_state_destroy(tg_grammar_state* s);
+/* Feed raw bytes, all or nothing (JSONSchemaFSM.acceptBytes). */
+int32_t tg_grammar_accept_bytes(tg_grammar_state* s, const uint8_t* bytes, int64_t n,
+                                int32_t* accepted);
+/* Advance by a sampled token's bytes (LogitsMasker.commit); *accepted = 0
+ * leaves the state unchanged. */
+int32_t tg_grammar_commit(tg_grammar_state* s, int32_t token, int32_t* accepted);
+int32_t tg_grammar_is_complete(const tg_grammar_state* s, int32_t* out);
+/* The state's mask into out_words[ceil(vocab/32)] (bit i%32 of word i/32 = token i). */
+int32_t tg_grammar_mask(const tg_grammar_state* s, uint32_t* out_words);
+/* The state's row in the grammar's mask table: automaton states with equal
+ * futures share a row; the row is computed and appended the first time such a
+ * state is seen (*is_new = 1).  The value to put in tg_sample's state_id. */
+int32_t tg_grammar_state_row(const tg_grammar_state* s, int32_t* row, int32_t* is_new);
+/* The host table (rows x ceil(vocab/32) words, row-major) to upload as
+ * tg_sample's mask_table; valid until the next tg_grammar_state_row. */
+int32_t tg_grammar_table(tg_grammar* g, const uint32_t** words, int32_t* rows);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

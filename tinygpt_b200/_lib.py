@@ -25,6 +25,8 @@ TG_MAX_VOCAB = 1 << 20
 TG_MAX_HISTORY = 4096
 TG_STATIC_SPEC_MAX_ROWS = 8192
 TG_SHARD_CAP = 1280
+TG_GRAMMAR_JSON_SCHEMA = 0
+TG_GRAMMAR_TOOL_TAGS = 1
 SHARD_RECORD_BYTES = 16 + 8 * TG_SHARD_CAP
 
 ROW_PARAMS_DTYPE = np.dtype([
@@ -35,7 +37,12 @@ ROW_PARAMS_DTYPE = np.dtype([
 
 EXPORTED = ["tg_abi_version", "tg_last_error_string", "tg_sampler_create", "tg_sampler_destroy",
             "tg_sample", "tg_sample_host", "tg_spec_verify", "tg_sampler_device_status", "tg_sampler_path_counters",
-            "tg_spec_verify_static", "tg_sample_shard_local", "tg_sample_shard_merge"]
+            "tg_spec_verify_static", "tg_sample_shard_local", "tg_sample_shard_merge",
+            "tg_grammar_last_error", "tg_grammar_create", "tg_grammar_destroy",
+            "tg_grammar_state_create", "tg_grammar_state_destroy", "tg_grammar_accept_bytes",
+            "tg_grammar_kind", "tg_grammar_state_clone",
+            "tg_grammar_commit", "tg_grammar_is_complete", "tg_grammar_mask",
+            "tg_grammar_state_row", "tg_grammar_table"]
 
 
 class TGError(RuntimeError):
@@ -82,6 +89,27 @@ def load(path: str = LIB_PATH):
     L.tg_sample_shard_local.restype = i32
     L.tg_sample_shard_merge.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp, vp, vp]
     L.tg_sample_shard_merge.restype = i32
+    L.tg_grammar_last_error.argtypes = []
+    L.tg_grammar_last_error.restype = ctypes.c_char_p
+    L.tg_grammar_create.argtypes = [ctypes.c_char_p, i64, i32, vp, vp, i32, ctypes.POINTER(vp)]
+    L.tg_grammar_destroy.argtypes = [vp]
+    L.tg_grammar_state_create.argtypes = [vp, ctypes.POINTER(vp)]
+    L.tg_grammar_state_destroy.argtypes = [vp]
+    L.tg_grammar_kind.argtypes = [vp, ctypes.POINTER(i32)]
+    L.tg_grammar_state_clone.argtypes = [vp, ctypes.POINTER(vp)]
+    L.tg_grammar_accept_bytes.argtypes = [vp, ctypes.c_char_p, i64, ctypes.POINTER(i32)]
+    L.tg_grammar_commit.argtypes = [vp, i32, ctypes.POINTER(i32)]
+    L.tg_grammar_is_complete.argtypes = [vp, ctypes.POINTER(i32)]
+    L.tg_grammar_mask.argtypes = [vp, vp]
+    L.tg_grammar_state_row.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
+    L.tg_grammar_table.argtypes = [vp, ctypes.POINTER(ctypes.POINTER(ctypes.c_uint32)),
+                                   ctypes.POINTER(i32)]
+    for name in ("tg_grammar_create", "tg_grammar_destroy", "tg_grammar_state_create",
+                 "tg_grammar_kind", "tg_grammar_state_clone",
+                 "tg_grammar_state_destroy", "tg_grammar_accept_bytes", "tg_grammar_commit",
+                 "tg_grammar_is_complete", "tg_grammar_mask", "tg_grammar_state_row",
+                 "tg_grammar_table"):
+        getattr(L, name).restype = i32
     _LIB = L
     return L
 

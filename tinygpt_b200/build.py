@@ -16,7 +16,7 @@ FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "--fm
 
 def sources() -> list[str]:
     return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC)
-                  if f.endswith((".cu", ".cuh")))
+                  if f.endswith((".cu", ".cuh", ".cpp")))
 
 
 def needs_build() -> bool:
@@ -29,7 +29,8 @@ def needs_build() -> bool:
 
 def build(force: bool = False, verbose: bool = False) -> str:
     if force or needs_build():
-        cmd = [NVCC, *FLAGS, "-o", LIB, os.path.join(CSRC, "tgsample.cu")]
+        cmd = [NVCC, *FLAGS, "-o", LIB, os.path.join(CSRC, "tgsample.cu"),
+               os.path.join(CSRC, "tg_grammar.cpp")]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         subprocess.run(cmd, check=True)
