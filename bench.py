@@ -34,7 +34,7 @@ B = 2048
 HIST = 512
 METRIC = "sampled rows/sec at V=128256 B=2048 bf16; % of HBM roofline at 1/2/4/8 GPU"
 BYTES_PER_ROW = V * 2 + HIST * 4  # logits once + history ids (258,560 B)
-PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "sample_kernel_config4.json")
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "stream_kernel_config4.json")
 
 
 def dist_env():
@@ -194,6 +194,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--profile-steps", type=int, default=50,
+                    help="untimed steps whose per-kernel CUDA-event times give the roofline")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":
@@ -257,9 +259,25 @@ def main():
     ms_max = float(t.item())
     rows = B * args.steps * world
     value = rows / (ms_max / 1e3)
-    ms_launch = ms / args.steps  # one kernel launch per step on this rank
-    achieved = B * BYTES_PER_ROW / (ms_launch / 1e3) / 1e9
     peak, peak_kind = measured_peak()
+    # per-kernel device times of the same steps (untimed pass, CUDA events
+    # recorded by the library around its kernels on the launching stream)
+    ktimes = []
+    s.profile(True)
+    for i in range(args.profile_steps):
+        step(i)
+        ktimes.append(s.profile(True))
+    s.profile(False)
+    nk = len(ktimes[-1])
+    kms = [float(np.mean([k[j] for k in ktimes])) for j in range(nk)]
+    if nk == 2:  # two-kernel mode: the streaming kernel reads the logits once
+        dom_ms, dom_bytes = kms[0], B * V * 2
+        dom_name, dom_share = "tg::sample_kernel<1, true> (streaming half)", kms[0] / (kms[0] + kms[1])
+    else:
+        dom_ms, dom_bytes = kms[0], B * BYTES_PER_ROW
+        dom_name, dom_share = "tg::sample_kernel<1>", 1.0
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    step_achieved = B * BYTES_PER_ROW / (ms / args.steps / 1e3) / 1e9
 
     # ---- e2e through the host-buffer entry point (pinned host memory) -------
     w = sets[0]
@@ -309,11 +327,16 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profile_traffic(),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-                         "kernel": "tg::sample_kernel<1>", "bytes_per_row": BYTES_PER_ROW},
+                         "kernel": dom_name, "kernel_ms": dom_ms, "kernel_share_of_step": dom_share,
+                         "algorithmic_bytes_per_launch": dom_bytes,
+                         "kernel_ms_all": kms,
+                         "step": {"achieved": step_achieved, "frac": step_achieved / peak,
+                                  "bytes_per_row": BYTES_PER_ROW,
+                                  "note": "whole step (every kernel) against the logits, history and id bytes"}},
             "e2e": {"value": e2e_val, "unit": "rows/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                     "path": "tg_sample_host, pinned host buffers"},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * nk,
             "clocks": clocks,
         }
         if cpu:

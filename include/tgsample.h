@@ -89,7 +89,10 @@ const char* tg_last_error_string(void);
 
 /* Create a sampler bound to CUDA device `device` for rows of `vocab` logits and
  * at most `max_batch` rows per call.  Allocates the device scratch and the host
- * staging used by the *_host variants.  Replaces tg_model_create's role as the
+ * staging used by the *_host variants; when vocab > 2816 and max_batch >= 256
+ * also the candidate buffer of the two-kernel mode, min(max_batch, 4096) rows of
+ * 22,536 bytes (92 MB at 4096 rows; environment TG_SAMPLE_SPLIT=0 at creation
+ * turns the mode and the buffer off).  Replaces tg_model_create's role as the
  * owner of sampling state (wasm/src/model.h:21-23); returns TG_OK and *out. */
 int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch,
                           tg_sampler** out);
@@ -238,6 +241,15 @@ int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits);
  * them when reset != 0. */
 #define TG_PATH_COUNTERS 8
 int32_t tg_sampler_path_counters(tg_sampler* s, uint64_t* out, int32_t n, int32_t reset);
+
+/* Kernel timing of tg_sample (diagnostics): with enable != 0 every later
+ * tg_sample call on this handle records CUDA events around its kernels.  Each
+ * call of this function first reports the last recorded call (synchronizing on
+ * it): *out_kernels = 2 with out_ms[0] the streaming and out_ms[1] the
+ * finishing kernel of the two-kernel mode, 1 with out_ms[0] the whole call, 0
+ * if none was recorded; then applies `enable`.  out_ms ([2]) and out_kernels
+ * may be NULL. */
+int32_t tg_sampler_profile(tg_sampler* s, int32_t enable, float* out_ms, int32_t* out_kernels);
 
 /* ---------------------------------------------------------------------------
  * Grammar compiler (host only; no GPU needed): grammar text -> byte-level

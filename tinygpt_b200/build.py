@@ -11,7 +11,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 # --fmad=false: the sampling semantics are defined op by op; no contraction.
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "--fmad=false",
-         "-std=c++17", "-Xcompiler", "-fPIC", "-shared", "-diag-suppress", "177"]
+         "-std=c++17", "-Xcompiler", "-fPIC", "-shared", "-diag-suppress", "177,128"]
 
 
 def sources() -> list[str]:

@@ -7,16 +7,26 @@
 namespace tg {
 
 constexpr unsigned kFull = 0xffffffffu;
+// Largest element count of a wide mass histogram: its 15-bit limb sums stay below 2^32.
+constexpr int kWideMassN = 1 << 16;
+
+__device__ __forceinline__ unsigned long long radix_mass_of(const unsigned int (&l)[4][256], int bin) {
+  return static_cast<unsigned long long>(l[0][bin]) + (static_cast<unsigned long long>(l[1][bin]) << 11) +
+         (static_cast<unsigned long long>(l[2][bin]) << 22) + (static_cast<unsigned long long>(l[3][bin]) << 33);
+}
 
 struct __align__(16) BlockScratch {
+  // Mass histograms are kept as 32-bit limbs of the 64-bit sums: shared-memory
+  // 32-bit atomic adds are native, 64-bit ones are compare-and-swap loops that
+  // serialise when lanes hit the same bin.
   union {
     struct {
-      unsigned long long hmass[256];
+      unsigned int hml[4][256];  // radix mass, 11-bit limbs (sums of up to 2^20 masses <= 2^44)
       unsigned int hcnt[256];
       unsigned int hfine[256];  // elements whose key has non-zero low 16 bits (kEarly16)
     };
     unsigned int hc[2048];        // wide count histogram (hist_round)
-    unsigned long long hm[1024];  // wide mass histogram (hist_round)
+    unsigned int hm3[3][1024];    // wide mass histogram, 15-bit limbs (at most kWideMassN masses)
   };
   unsigned long long red_u64[32];
   float red_f[32];
@@ -185,7 +195,11 @@ __device__ __forceinline__ void hist_zero(BlockScratch& sm) {
   constexpr int P = NB / NT;
 #pragma unroll
   for (int j = 0; j < P; j++) {
-    if (kMass) sm.hm[threadIdx.x * P + j] = 0ull;
+    if (kMass) {
+      sm.hm3[0][threadIdx.x * P + j] = 0u;
+      sm.hm3[1][threadIdx.x * P + j] = 0u;
+      sm.hm3[2][threadIdx.x * P + j] = 0u;
+    }
     else sm.hc[threadIdx.x * P + j] = 0u;
   }
   if (threadIdx.x == 0) sm.sel_bin = 0xffffffffu;
@@ -193,8 +207,13 @@ __device__ __forceinline__ void hist_zero(BlockScratch& sm) {
 
 template <bool kMass>
 __device__ __forceinline__ void hist_put(BlockScratch& sm, int bin, unsigned long long w) {
-  if (kMass) atomicAdd(&sm.hm[bin], w);
-  else atomicAdd(&sm.hc[bin], 1u);
+  if (kMass) {  // w <= 2^44
+    atomicAdd(&sm.hm3[0][bin], static_cast<unsigned>(w & 0x7fffu));
+    atomicAdd(&sm.hm3[1][bin], static_cast<unsigned>((w >> 15) & 0x7fffu));
+    atomicAdd(&sm.hm3[2][bin], static_cast<unsigned>(w >> 30));
+  } else {
+    atomicAdd(&sm.hc[bin], 1u);
+  }
 }
 
 template <int NT, int NB, bool kMass, class Reached>
@@ -206,7 +225,10 @@ __device__ HistSel hist_scan(Reached reached, BlockScratch& sm) {
   unsigned long long loc = 0;
 #pragma unroll
   for (int j = 0; j < P; j++) {
-    v[j] = kMass ? sm.hm[t * P + j] : static_cast<unsigned long long>(sm.hc[t * P + j]);
+    const int b = t * P + j;
+    v[j] = kMass ? static_cast<unsigned long long>(sm.hm3[0][b]) + (static_cast<unsigned long long>(sm.hm3[1][b]) << 15) +
+                       (static_cast<unsigned long long>(sm.hm3[2][b]) << 30)
+                 : static_cast<unsigned long long>(sm.hc[b]);
     loc += v[j];
   }
   unsigned long long tot;
@@ -303,16 +325,18 @@ template <bool kMass>
 __device__ __forceinline__ void hist_add(BlockScratch& sm, uint32_t d, unsigned long long w) {
   const unsigned act = __activemask();
   const unsigned peers = __match_any_sync(act, d);
-  if (kMass) {  // sum of w over the peers, in three 22-bit slices (no u32 overflow)
-    const unsigned lo = __reduce_add_sync(peers, static_cast<unsigned>(w & 0x3fffffull));
-    const unsigned mid = __reduce_add_sync(peers, static_cast<unsigned>((w >> 22) & 0x3fffffull));
-    const unsigned hi = __reduce_add_sync(peers, static_cast<unsigned>(w >> 44));
-    w = static_cast<unsigned long long>(lo) + (static_cast<unsigned long long>(mid) << 22) +
-        (static_cast<unsigned long long>(hi) << 44);
+  unsigned l[4] = {0u, 0u, 0u, 0u};
+  if (kMass) {  // w <= 2^44: four 11-bit limbs, each summed over the peers
+#pragma unroll
+    for (int i = 0; i < 4; i++) l[i] = __reduce_add_sync(peers, static_cast<unsigned>((w >> (11 * i)) & (i == 3 ? 0xfffu : 0x7ffu)));
   }
   if ((threadIdx.x & 31) == __ffs(peers) - 1) {
     atomicAdd(&sm.hcnt[d], static_cast<unsigned>(__popc(peers)));
-    if (kMass) atomicAdd(&sm.hmass[d], w);
+    if (kMass) {
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (l[i]) atomicAdd(&sm.hml[i][d], l[i]);
+    }
   }
 }
 
@@ -347,7 +371,7 @@ __device__ void radix_find(const Src& src, int nbits, KeyW keyw, Reached reached
     const uint32_t dmask = (1u << width) - 1u;
     const bool fine_round = kEarly16 && shift == 16;
     for (int i = threadIdx.x; i < 256; i += NT) {
-      sm.hmass[i] = 0ull;
+      sm.hml[0][i] = 0u; sm.hml[1][i] = 0u; sm.hml[2][i] = 0u; sm.hml[3][i] = 0u;
       sm.hcnt[i] = 0u;
       if (fine_round) sm.hfine[i] = 0u;
     }
@@ -371,7 +395,7 @@ __device__ void radix_find(const Src& src, int nbits, KeyW keyw, Reached reached
         const int p = lane * per + q;
         if (p < nb) {
           const int bin = kDesc ? nb - 1 - p : p;
-          lm += kMass ? sm.hmass[bin] : 0ull;
+          lm += kMass ? radix_mass_of(sm.hml, bin) : 0ull;
           lc += sm.hcnt[bin];
         }
       }
@@ -393,7 +417,7 @@ __device__ void radix_find(const Src& src, int nbits, KeyW keyw, Reached reached
         const int p = lane * per + q;
         if (p < nb) {
           const int bin = kDesc ? nb - 1 - p : p;
-          const unsigned long long m = kMass ? sm.hmass[bin] : 0ull;
+          const unsigned long long m = kMass ? radix_mass_of(sm.hml, bin) : 0ull;
           const unsigned int c = sm.hcnt[bin];
           if (c > 0) {
             if (found < 0 && reached(cm + m, cc + c)) { found = bin; fb = cm; fcb = cc; }
@@ -419,7 +443,7 @@ __device__ void radix_find(const Src& src, int nbits, KeyW keyw, Reached reached
       __syncwarp();
       if (lane == 0) {
         sm.sel_cnt = sm.hcnt[sm.sel_bin];
-        sm.sel_mass = kMass ? sm.hmass[sm.sel_bin] : 0ull;
+        sm.sel_mass = kMass ? radix_mass_of(sm.hml, sm.sel_bin) : 0ull;
       }
     }
     __syncthreads();

@@ -101,6 +101,22 @@ struct Elt<1> {  // bf16
     asm("max.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(a), "r"(b));
     return fmaxf(bf16_lo(m), bf16_hi(m));
   }
+  // max over N vectors: a packed bf16x2 tree, one fp32 max at the end
+  template <int N>
+  __device__ __forceinline__ static float vmax_n(const uint4* w) {
+    uint32_t r[2 * N];
+#pragma unroll
+    for (int q = 0; q < N; q++) {
+      asm("max.bf16x2 %0, %1, %2;" : "=r"(r[2 * q]) : "r"(w[q].x), "r"(w[q].y));
+      asm("max.bf16x2 %0, %1, %2;" : "=r"(r[2 * q + 1]) : "r"(w[q].z), "r"(w[q].w));
+    }
+#pragma unroll
+    for (int n = 2 * N; n > 1; n >>= 1) {
+#pragma unroll
+      for (int i = 0; i < n / 2; i++) asm("max.bf16x2 %0, %1, %2;" : "=r"(r[i]) : "r"(r[2 * i]), "r"(r[2 * i + 1]));
+    }
+    return fmaxf(bf16_lo(r[0]), bf16_hi(r[0]));
+  }
 };
 
 template <>
@@ -117,6 +133,13 @@ struct Elt<0> {  // fp32
   __device__ __forceinline__ static float vmax(const uint4& w) {
     return fmaxf(fmaxf(__uint_as_float(w.x), __uint_as_float(w.y)),
                  fmaxf(__uint_as_float(w.z), __uint_as_float(w.w)));
+  }
+  template <int N>
+  __device__ __forceinline__ static float vmax_n(const uint4* w) {
+    float m = vmax(w[0]);
+#pragma unroll
+    for (int q = 1; q < N; q++) m = fmaxf(m, vmax(w[q]));
+    return m;
   }
 };
 

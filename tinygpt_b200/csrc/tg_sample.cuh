@@ -29,8 +29,14 @@
 
 namespace tg {
 
-constexpr int kSampleNT = 256;   // threads per CTA
-constexpr int kCandMax = 3072;   // candidate list capacity
+#ifndef TG_NT
+#define TG_NT 256
+#endif
+#ifndef TG_CAND_MAX
+#define TG_CAND_MAX 2816
+#endif
+constexpr int kSampleNT = TG_NT;        // threads per CTA
+constexpr int kCandMax = TG_CAND_MAX;   // candidate list capacity
 constexpr int kFastMaxK = 1024;  // largest top-k served by the candidate path
 constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold sample
 #ifndef TG_UNROLL
@@ -43,8 +49,18 @@ constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) befo
 #define TG_MIN_CTAS 4
 #endif
 constexpr int kMinCtasPerSm = TG_MIN_CTAS;  // occupancy target (4: registers capped at 64)
+#ifndef TG_STREAM_CTAS
+#define TG_STREAM_CTAS 5
+#endif
+constexpr int kStreamCtasPerSm = TG_STREAM_CTAS;  // occupancy of the streaming kernel
+// Candidate target of the threshold: the sample estimates the element of rank
+// kTgtMul * k + kTgtAdd; the margin over k absorbs the sample's error (tighter
+// margins measured slower: more rows needed a second pass).
+constexpr float kTgtMul = 1.5f;
+constexpr float kTgtAdd = 96.0f;
 constexpr int kRing = 64;  // hit-vector ring entries per warp (drained at 32)
 static_assert((kSampleNT / 32) * kRing * 20 <= kCandMax * 4, "rings must fit in cand_e");
+static_assert(kCandMax <= kWideMassN, "candidate mass histograms must not overflow their limbs");
 
 // Diagnostic build only (-DTG_PHASE_TIMING): cycles per phase summed over CTAs.
 #ifdef TG_PHASE_TIMING
@@ -90,6 +106,13 @@ struct SampleArgs {
   int32_t vocab_offset;
   int32_t full_vocab;
   tg_shard_record* shard_out;
+  // two-kernel mode: the streaming kernel leaves each row's raw candidate list
+  // (every element >= theta, kCandMax slots per row), its length (-1: row not
+  // streamed) and theta here; the finishing kernel starts from them
+  float* cand_gy;
+  int32_t* cand_gid;
+  int32_t* cand_gn;
+  float* cand_gth;
 };
 
 // History hash in shared memory: key = token id (-1 empty); val = count, then
@@ -748,8 +771,10 @@ __device__ void shard_emit(const Src& src, const tg_row_params& p, int V, int mo
   __syncthreads();
 }
 
-template <int DT>
-__global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(SampleArgs a) {
+// kStream: the streaming half of the two-kernel mode (threshold, streaming
+// pass, raw candidates to global memory); no history, no selection code.
+template <int DT, bool kStream = false>
+__global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCtasPerSm) sample_kernel(SampleArgs a) {
   using E = Elt<DT>;
   constexpr int EPV = E::kEPV;
   constexpr int SV = kSampleVecs;
@@ -760,9 +785,18 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   const int t = threadIdx.x;
   const int moff = a.vocab_offset;  // global id of this shard's element 0
   const int V = a.vocab;
-  float* cand_y = reinterpret_cast<float*>(dyn);
-  int* cand_id = reinterpret_cast<int*>(dyn + kCandMax * 4);
-  float* cand_e = reinterpret_cast<float*>(dyn + kCandMax * 8);
+  float* cand_y;
+  int* cand_id;
+  float* cand_e;
+  if constexpr (kStream) {  // list in global memory; the warps' rings are the shared memory
+    cand_y = a.cand_gy + static_cast<int64_t>(b) * kCandMax;
+    cand_id = a.cand_gid + static_cast<int64_t>(b) * kCandMax;
+    cand_e = reinterpret_cast<float*>(dyn);
+  } else {
+    cand_y = reinterpret_cast<float*>(dyn);
+    cand_id = reinterpret_cast<int*>(dyn + kCandMax * 4);
+    cand_e = reinterpret_cast<float*>(dyn + kCandMax * 8);
+  }
   int* hkey = reinterpret_cast<int*>(dyn + kCandMax * 12);
   const int ht = a.ht_log2 ? (1 << a.ht_log2) : 0;
   int* hval = hkey + ht;
@@ -777,6 +811,10 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   if (a.mask_table && a.state_id) {
     const int sid = a.state_id[b];
     if (sid >= a.num_states) {
+      if constexpr (kStream) {  // the finishing kernel reports it
+        if (t == 0) a.cand_gn[b] = -1;
+        return;
+      }
       if (t == 0) {
         if (a.shard_out) {
           a.shard_out[b].count = -1;
@@ -808,7 +846,7 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   const bool rep_on = p.repetition_penalty > 1.0f;
   const bool pf_on = p.presence_penalty != 0.0f || p.frequency_penalty != 0.0f;
   Hist hist{hkey, hval, bloom, ht - 1, a.ht_log2, 0};
-  const bool need_hist = hlen > 0 && (rep_on || pf_on);
+  const bool need_hist = !kStream && hlen > 0 && (rep_on || pf_on);
 
   // (a) history -> shared hash of penalised values (raw values read from L2
   // when this runs after the streaming pass)
@@ -874,11 +912,19 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
   int out_id = -1;
   float out_prob = 0.0f;
   bool done = false;
+  if constexpr (kStream) {
+    if (!fast) {
+      if (t == 0) a.cand_gn[b] = -1;
+      return;
+    }
+  }
+  // two-kernel mode: this row's candidates were streamed already
+  const bool pre = !kStream && a.cand_gn != nullptr && a.cand_gn[b] >= 0;
 
   if (fast) {
     const int keff = greedy ? 1 : (topk ? p.top_k : V);
     const unsigned int need = static_cast<unsigned int>(keff < V ? keff : 1);
-    const float tgt = 1.5f * static_cast<float>(keff < V ? keff : kNoTopkTarget) + 96.0f;
+    const float tgt = kTgtMul * static_cast<float>(keff < V ? keff : kNoTopkTarget) + kTgtAdd;
     const int lane = t & 31, warp = t >> 5;
     const unsigned lt = (1u << lane) - 1u;
 
@@ -967,13 +1013,8 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
     // bytes; a warp ballot sends the vectors holding an element >= th to the ring.
     auto scan = [&](float th, int j0) {
       int rcnt = 0;  // warp-uniform ring fill
-      for (int jb = j0; jb < nvec; jb += kUnroll * kSampleNT) {
-        uint4 w[kUnroll];
-#pragma unroll
-        for (int q = 0; q < kUnroll; q++) {
-          const int j = jb + q * kSampleNT + t;
-          if (j < nvec) w[q] = ldg_stream(vrow + j);
-        }
+      // exact per-vector test of one group; hit vectors go to the ring
+      auto group = [&](const uint4* w, int jb) {
 #pragma unroll
         for (int q = 0; q < kUnroll; q++) {
           if (jb + q * kSampleNT >= nvec) break;  // warp-uniform
@@ -990,6 +1031,27 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
             if (rcnt >= 32) { drain(rcnt, th); rcnt = 0; }
           }
         }
+      };
+      int jb = j0;
+      if (!mask) {
+        // full groups: no bounds checks, and one packed max over the lane's
+        // vectors decides whether the warp needs the exact per-vector test
+        for (; jb + kUnroll * kSampleNT <= nvec; jb += kUnroll * kSampleNT) {
+          const uint4* pv = vrow + jb + t;
+          uint4 w[kUnroll];
+#pragma unroll
+          for (int q = 0; q < kUnroll; q++) w[q] = ldg_stream(pv + q * kSampleNT);
+          if (__any_sync(kFull, E::template vmax_n<kUnroll>(w) >= th)) group(w, jb);
+        }
+      }
+      for (; jb < nvec; jb += kUnroll * kSampleNT) {
+        uint4 w[kUnroll];
+#pragma unroll
+        for (int q = 0; q < kUnroll; q++) {
+          const int j = jb + q * kSampleNT + t;
+          if (j < nvec) w[q] = ldg_stream(vrow + j);
+        }
+        group(w, jb);
       }
       if (rcnt) drain(rcnt, th);
     };
@@ -1010,7 +1072,24 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
     float theta = neg_inf();
     unsigned int rk = 0;
     bool fits;
-    {
+    if (pre) {
+      pc.mark(0);
+      if (!risers) build_hist(0.0f, false);
+      if (V > kCandMax && sampled > 0) rk = rank_for(1.0f);
+      theta = a.cand_gth[b];
+      const int n = a.cand_gn[b];
+      const int m = n < kCandMax ? n : kCandMax;
+      const float* gy = a.cand_gy + static_cast<int64_t>(b) * kCandMax;
+      const int* gid = a.cand_gid + static_cast<int64_t>(b) * kCandMax;
+      for (int i = t; i < m; i += kSampleNT) {
+        cand_y[i] = __ldcs(gy + i);
+        cand_id[i] = __ldcs(gid + i);
+      }
+      if (t == 0) sm.cand_count = n;
+      __syncthreads();
+      fits = true;
+      pc.mark(1);
+    } else {
       uint4 raw[SV];
       float vm[SV];
       pc.mark(0);
@@ -1038,11 +1117,18 @@ __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_kernel(Sample
         const int j = t + q * kSampleNT;
         if (j < nvec && vm[q] >= theta) append_vec(raw[q], j, theta);
       }
+      scalars(theta);
+      scan(theta, SV * kSampleNT);
+      fits = expand(theta);
     }
-    scalars(theta);
-    scan(theta, SV * kSampleNT);
-    fits = expand(theta);
     pc.mark(2);
+    if constexpr (kStream) {
+      if (t == 0) {
+        a.cand_gn[b] = sm.cand_count;
+        a.cand_gth[b] = theta;
+      }
+      return;
+    }
 
     for (int attempt = 0;; attempt++) {
       if (need_hist) {

@@ -106,8 +106,23 @@ struct tg_sampler {
   // staging for tg_sample_host
   DevBuf h_logits, h_params, h_hist, h_hlen, h_mask, h_state, h_unif, h_out, h_prob;
   cudaStream_t stream = nullptr;  // used by tg_sample_host only
+  // two-kernel mode: raw candidate lists of up to split_rows rows per launch pair
+  DevBuf cand;
+  int split_rows = 0;  // 0: single-kernel mode
+  // tg_sampler_profile: events around the kernels of the last tg_sample call
+  bool profile = false;
+  cudaEvent_t prof_ev[3] = {nullptr, nullptr, nullptr};
+  int prof_kind = 0;  // 0: no call recorded, 1: one kernel, 2: two kernels
   std::mutex mu;
 };
+
+namespace {
+// Rows per streaming / finishing launch pair (bounds the candidate buffer:
+// kCandMax * 8 + 8 bytes per row).
+constexpr int kSplitRows = 4096;
+// The two-kernel mode pays for itself from this many rows on.
+constexpr int kSplitMinBatch = 256;
+}  // namespace
 
 extern "C" {
 
@@ -138,6 +153,14 @@ int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_s
     e = cudaFuncSetAttribute(tg::sample_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tg::sample_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  // the two-kernel mode serves rows longer than a candidate list, in batches of
+  // kSplitMinBatch rows or more (TG_SAMPLE_SPLIT=0 turns it off)
+  const char* split_env = getenv("TG_SAMPLE_SPLIT");
+  if (e == cudaSuccess && vocab > tg::kCandMax && max_batch >= kSplitMinBatch &&
+      !(split_env && split_env[0] == '0')) {
+    s->split_rows = max_batch < kSplitRows ? max_batch : kSplitRows;
+    e = s->cand.ensure(static_cast<size_t>(s->split_rows) * (static_cast<size_t>(tg::kCandMax) * 8 + 8));
+  }
   if (e != cudaSuccess) {
     tg_sampler_destroy(s);
     return cuda_fail(e, "tg_sampler_create");
@@ -153,6 +176,9 @@ int32_t tg_sampler_destroy(tg_sampler* s) {
     if (s->d_status) cudaFree(s->d_status);
     if (s->d_counters) cudaFree(s->d_counters);
     s->stats.release();
+    s->cand.release();
+    for (cudaEvent_t ev : s->prof_ev)
+      if (ev) cudaEventDestroy(ev);
     for (DevBuf* b : {&s->h_logits, &s->h_params, &s->h_hist, &s->h_hlen, &s->h_mask, &s->h_state,
                       &s->h_unif, &s->h_out, &s->h_prob})
       b->release();
@@ -210,11 +236,66 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
   const size_t smem = static_cast<size_t>(tg::kCandMax) * 12 + (a.ht_log2 ? (size_t(8) << a.ht_log2) : 0);
   DeviceGuard g(s->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == TG_DTYPE_F32)
-    tg::sample_kernel<0><<<batch, tg::kSampleNT, smem, st>>>(a);
-  else
-    tg::sample_kernel<1><<<batch, tg::kSampleNT, smem, st>>>(a);
-  TG_CUDA(cudaGetLastError());
+  if (s->profile) TG_CUDA(cudaEventRecord(s->prof_ev[0], st));
+  if (s->split_rows == 0 || batch < kSplitMinBatch) {
+    if (dtype == TG_DTYPE_F32)
+      tg::sample_kernel<0><<<batch, tg::kSampleNT, smem, st>>>(a);
+    else
+      tg::sample_kernel<1><<<batch, tg::kSampleNT, smem, st>>>(a);
+    TG_CUDA(cudaGetLastError());
+    if (s->profile) {
+      TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
+      s->prof_kind = 1;
+    }
+    return TG_OK;
+  }
+  // two-kernel mode, split_rows rows per launch pair: the streaming kernel
+  // (rings in shared memory, high occupancy) leaves the raw candidates of each
+  // row in s->cand; the finishing kernel then selects from them.  Running the
+  // pair back to back beat running chunks of the two concurrently, which
+  // split the SMs between them.
+  const int R = s->split_rows;
+  char* cb = static_cast<char*>(s->cand.p);
+  a.cand_gy = reinterpret_cast<float*>(cb);
+  a.cand_gid = reinterpret_cast<int32_t*>(cb + static_cast<size_t>(R) * tg::kCandMax * 4);
+  a.cand_gn = reinterpret_cast<int32_t*>(cb + static_cast<size_t>(R) * tg::kCandMax * 8);
+  a.cand_gth = reinterpret_cast<float*>(cb + static_cast<size_t>(R) * (tg::kCandMax * 8 + 4));
+  const size_t ring_smem = static_cast<size_t>(tg::kSampleNT / 32) * tg::kRing * 20;
+  const int64_t es = dtype == TG_DTYPE_F32 ? 4 : 2;
+  for (int32_t r0 = 0; r0 < batch; r0 += R) {
+    const int32_t n = batch - r0 < R ? batch - r0 : R;
+    tg::SampleArgs c = a;
+    c.batch = n;
+    c.logits = static_cast<const char*>(logits) + r0 * row_stride * es;
+    c.params = params + r0;
+    if (c.history) c.history = history + static_cast<int64_t>(r0) * history_stride;
+    if (c.history_len) c.history_len = history_len + r0;
+    if (c.state_id) c.state_id = state_id + r0;
+    if (c.uniforms) c.uniforms = uniforms + r0;
+    if (c.out_ids) c.out_ids = out_ids + r0;
+    if (c.out_probs) c.out_probs = out_probs + r0;
+    if (c.shard_out) c.shard_out = shard_out + r0;
+    const bool mark = s->profile && r0 == 0 && n == batch;  // single launch pair: time each kernel
+    if (dtype == TG_DTYPE_F32)
+      tg::sample_kernel<0, true><<<n, tg::kSampleNT, ring_smem, st>>>(c);
+    else
+      tg::sample_kernel<1, true><<<n, tg::kSampleNT, ring_smem, st>>>(c);
+    if (mark) TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
+    if (dtype == TG_DTYPE_F32)
+      tg::sample_kernel<0><<<n, tg::kSampleNT, smem, st>>>(c);
+    else
+      tg::sample_kernel<1><<<n, tg::kSampleNT, smem, st>>>(c);
+    TG_CUDA(cudaGetLastError());
+  }
+  if (s->profile) {
+    if (batch <= R) {
+      TG_CUDA(cudaEventRecord(s->prof_ev[2], st));
+      s->prof_kind = 2;
+    } else {  // several launch pairs: the whole call only
+      TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
+      s->prof_kind = 1;
+    }
+  }
   return TG_OK;
 }
 
@@ -419,6 +500,30 @@ int32_t tg_sampler_path_counters(tg_sampler* s, uint64_t* out, int32_t n, int32_
   TG_CUDA(cudaMemcpy(tmp, s->d_counters, sizeof(tmp), cudaMemcpyDeviceToHost));
   for (int i = 0; i < n && i < TG_PATH_COUNTERS; i++) out[i] = tmp[i];
   if (reset) TG_CUDA(cudaMemset(s->d_counters, 0, sizeof(tmp)));
+  return TG_OK;
+}
+
+int32_t tg_sampler_profile(tg_sampler* s, int32_t enable, float* out_ms, int32_t* out_kernels) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  DeviceGuard g(s->device);
+  if (enable && !s->prof_ev[0]) {
+    for (cudaEvent_t& ev : s->prof_ev) TG_CUDA(cudaEventCreate(&ev));
+  }
+  if (out_ms || out_kernels) {
+    int n = 0;
+    if (s->prof_kind > 0) {
+      TG_CUDA(cudaEventSynchronize(s->prof_ev[s->prof_kind]));
+      for (int i = 0; i < s->prof_kind; i++) {
+        float ms = 0.0f;
+        TG_CUDA(cudaEventElapsedTime(&ms, s->prof_ev[i], s->prof_ev[i + 1]));
+        if (out_ms) out_ms[i] = ms;
+      }
+      n = s->prof_kind;
+    }
+    if (out_kernels) *out_kernels = n;
+  }
+  s->profile = enable != 0;
+  if (!s->profile) s->prof_kind = 0;
   return TG_OK;
 }
 

@@ -207,6 +207,15 @@ class Sampler:
         keys = ["candidate", "overflow", "short", "threshold", "full_row", "candidates"]
         return {k: int(buf[i]) for i, k in enumerate(keys)}
 
+    def profile(self, enable: bool = True):
+        """Kernel times (ms) of the last tg_sample call recorded while profiling
+        was on: (stream, finish) in the two-kernel mode, (whole call,) otherwise;
+        then switches recording on or off (tg_sampler_profile)."""
+        ms = (ctypes.c_float * 2)()
+        n = ctypes.c_int32(0)
+        check(self._L.tg_sampler_profile(self._h, int(enable), ms, ctypes.byref(n)))
+        return tuple(ms[i] for i in range(n.value))
+
     def device_status(self) -> int:
         bits = ctypes.c_uint32(0)
         check(self._L.tg_sampler_device_status(self._h, ctypes.byref(bits)))
