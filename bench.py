@@ -186,6 +186,99 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_config(args):
+    """One JSON line for one of the five workloads (`--config N`, one GPU): the
+    device time of a tg_sample / tg_spec_verify call on resident inputs, CUDA
+    events over `--steps` calls (config 1: calls replayed from a CUDA graph, the
+    latency of one call).  Inputs come from tinygpt_b200.workloads (the
+    oracle-checked workloads); configs 3-5 exceed L2 (two sets alternate for 3
+    and 4; config 5 is 722 MB per call), configs 1-2 are L2-resident."""
+    import torch
+    from tinygpt_b200 import workloads as W
+    from tinygpt_b200.sampler import Sampler, params_to_device
+    cfg = args.config
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    c = W.CONFIGS[cfg]
+    Vc, Bc = c["vocab"], c["batch"]
+    s = Sampler(Vc, Bc, 0)
+    sets = [W.make(cfg, seed=1 + i) for i in range(2 if cfg in (3, 4) else 1)]
+
+    def to_dev(w):
+        d = {}
+        if cfg == 5:
+            d["t"] = torch.from_numpy(w["target"].astype(np.float32)).to(dev)
+            d["d"] = torch.from_numpy(w["draft"].astype(np.float32)).to(dev)
+            for k in ("draft_ids", "temperature", "u_accept", "u_draw"):
+                d[k] = torch.from_numpy(np.ascontiguousarray(w[k])).to(dev)
+            return d
+        x = w["logits"]
+        t = torch.from_numpy(np.ascontiguousarray(x))
+        if x.dtype == np.uint16:
+            t = t.view(torch.int16).view(torch.bfloat16)
+        opt = lambda k: torch.from_numpy(w[k]).to(dev) if w.get(k) is not None else None  # noqa: E731
+        d.update(x=t.to(dev), p=params_to_device(w["params"], dev), u=opt("uniforms"),
+                 h=opt("history"), hl=opt("history_len"), sid=opt("state_id"),
+                 m=torch.from_numpy(w["mask_table"].view(np.int32)).to(dev) if w.get("mask_table") is not None else None)
+        return d
+
+    ds = [to_dev(w) for w in sets]
+    out = torch.empty(Bc, dtype=torch.int32, device=dev)
+
+    def call(i):
+        d = ds[i % len(ds)]
+        st = torch.cuda.current_stream()
+        if cfg == 5:
+            s.spec_verify(d["t"], d["d"], d["draft_ids"], d["temperature"], d["u_accept"], d["u_draw"], stream=st)
+        else:
+            s.sample(d["x"], d["p"], history=d["h"], history_len=d["hl"], mask_table=d["m"],
+                     state_id=d["sid"], uniforms=d["u"], out=out, stream=st)
+
+    for i in range(max(args.warmup, 3)):
+        call(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if cfg == 1:  # latency: a graph of G calls, replayed
+        G = 100
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(G):
+                call(i)
+        g.replay()
+        torch.cuda.synchronize()
+        reps = max(1, args.steps // G)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        calls = reps * G
+    else:
+        e0.record(stream)
+        for i in range(args.steps):
+            call(i)
+        e1.record(stream)
+        calls = args.steps
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / calls
+    peak, peak_kind = measured_peak()
+    bytes_call = W.bytes_per_row(cfg) * Bc
+    achieved = bytes_call / (us * 1e-6) / 1e9
+    line = {"metric": f"config {cfg} ({c['name']}): device time per call", "value": us, "unit": "us",
+            "higher_is_better": False, "n_gpus": 1, "steps": calls, "warmup": args.warmup,
+            "rows_per_s": Bc / (us * 1e-6), "dtype": c["dtype"],
+            "data": "synthetic (tinygpt_b200.workloads, seeded Philox)",
+            "config": {"workload": f"config {cfg}", "vocab": Vc, "batch": Bc,
+                       "l2": "inputs larger than L2, two sets alternate" if cfg in (3, 4) else
+                             ("722 MB per call, larger than L2" if cfg == 5 else "L2-resident (latency-bound size)"),
+                       "timing": "CUDA graph of 100 calls, replayed" if cfg == 1 else "CUDA events over back-to-back calls"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "algorithmic_bytes_per_call": bytes_call,
+                         "peak_source": peak_kind}}
+    print(json.dumps(line), flush=True)
+    s.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -196,7 +289,12 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--profile-steps", type=int, default=50,
                     help="untimed steps whose per-kernel CUDA-event times give the roofline")
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
+                    help="1-5: one line for that workload's call time (one GPU) instead of the headline")
     args = ap.parse_args()
+    if args.config:
+        run_config(args)
+        return
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)

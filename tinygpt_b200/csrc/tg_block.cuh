@@ -45,8 +45,16 @@ struct __align__(16) BlockScratch {
   float red_f2[32];
 };
 
-template <int NT>
-__device__ __forceinline__ float block_max(float v, BlockScratch& sm) {
+// Reductions need only the red_* fields: S is BlockScratch or ReduceScratch.
+struct ReduceScratch {
+  unsigned long long red_u64[32];
+  float red_f[32];
+  int red_i[32];
+  float red_f2[32];
+};
+
+template <int NT, class S>
+__device__ __forceinline__ float block_max(float v, S& sm) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
   if ((threadIdx.x & 31) == 0) sm.red_f[threadIdx.x >> 5] = v;
   __syncthreads();
@@ -58,8 +66,8 @@ __device__ __forceinline__ float block_max(float v, BlockScratch& sm) {
 }
 
 // Two maxima with one pair of barriers.
-template <int NT>
-__device__ __forceinline__ void block_max2(float& a, float& b, BlockScratch& sm) {
+template <int NT, class S>
+__device__ __forceinline__ void block_max2(float& a, float& b, S& sm) {
   for (int o = 16; o > 0; o >>= 1) {
     a = fmaxf(a, __shfl_xor_sync(kFull, a, o));
     b = fmaxf(b, __shfl_xor_sync(kFull, b, o));
@@ -73,8 +81,8 @@ __device__ __forceinline__ void block_max2(float& a, float& b, BlockScratch& sm)
   __syncthreads();
 }
 
-template <int NT>
-__device__ __forceinline__ unsigned long long block_sum(unsigned long long v, BlockScratch& sm) {
+template <int NT, class S>
+__device__ __forceinline__ unsigned long long block_sum(unsigned long long v, S& sm) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
   if ((threadIdx.x & 31) == 0) sm.red_u64[threadIdx.x >> 5] = v;
   __syncthreads();
@@ -85,8 +93,8 @@ __device__ __forceinline__ unsigned long long block_sum(unsigned long long v, Bl
   return r;
 }
 
-template <int NT>
-__device__ __forceinline__ unsigned int block_max_u32(unsigned int v, BlockScratch& sm) {
+template <int NT, class S>
+__device__ __forceinline__ unsigned int block_max_u32(unsigned int v, S& sm) {
   for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(kFull, v, o));
   if ((threadIdx.x & 31) == 0) sm.red_i[threadIdx.x >> 5] = static_cast<int>(v);
   __syncthreads();
@@ -98,8 +106,8 @@ __device__ __forceinline__ unsigned int block_max_u32(unsigned int v, BlockScrat
 }
 
 // Max y, then the smallest id holding it.  Returns via references.
-template <int NT>
-__device__ __forceinline__ void block_argmax(float& y, int& id, BlockScratch& sm) {
+template <int NT, class S>
+__device__ __forceinline__ void block_argmax(float& y, int& id, S& sm) {
   for (int o = 16; o > 0; o >>= 1) {
     const float oy = __shfl_xor_sync(kFull, y, o);
     const int oi = __shfl_xor_sync(kFull, id, o);
@@ -122,10 +130,10 @@ __device__ __forceinline__ void block_argmax(float& y, int& id, BlockScratch& sm
 }
 
 // Exclusive prefix sum of one u64 per thread in thread order; also the total.
-template <int NT>
+template <int NT, class S>
 __device__ __forceinline__ unsigned long long block_excl_scan(unsigned long long v,
                                                               unsigned long long& total,
-                                                              BlockScratch& sm) {
+                                                              S& sm) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   unsigned long long incl = v;
   for (int o = 1; o < 32; o <<= 1) {

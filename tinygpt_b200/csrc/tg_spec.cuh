@@ -118,7 +118,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   using E = Elt<DT>;
   extern __shared__ __align__(128) unsigned char slice[];
   __shared__ __align__(8) uint64_t bar;
-  __shared__ BlockScratch sm;
+  __shared__ ReduceScratch sm;
   __shared__ float c_max;
   __shared__ int c_arg;
   __shared__ unsigned long long c_z;
@@ -269,7 +269,7 @@ template <int DT>
 __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     spec_verify_kernel(SpecArgs a) {
   using E = Elt<DT>;
-  __shared__ BlockScratch sm;
+  __shared__ ReduceScratch sm;
   __shared__ int s_fin, s_n;  // rank 0: the rejecting position (-1 bonus, -2 done) and accepted count
   __shared__ unsigned long long c_sumT, c_sumR;
   cg::cluster_group cluster = cg::this_cluster();

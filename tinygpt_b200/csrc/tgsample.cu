@@ -121,7 +121,7 @@ namespace {
 // kCandMax * 8 + 8 bytes per row).
 constexpr int kSplitRows = 4096;
 // The two-kernel mode pays for itself from this many rows on.
-constexpr int kSplitMinBatch = 256;
+constexpr int kSplitMinBatch = 1024;
 }  // namespace
 
 extern "C" {
