@@ -158,6 +158,25 @@ int32_t tg_spec_verify(tg_sampler* s, const void* target_logits,
                        const float* u_draw, int32_t* out_ids, int32_t* out_n,
                        void* stream);
 
+/* Grammar-masked verification: tg_spec_verify under the constraint of a
+ * grammar (mask table as in tg_sample, rows from tg_grammar_state_row).
+ * state_ids [batch, K+1] int32 device array: the grammar state before the token
+ * of each position (position i's state follows the draft tokens 0..i-1; -1 =
+ * unmasked position).  At position i an element whose bit is clear counts as
+ * -inf in both the target and the draft rows, so both distributions are
+ * renormalised over the allowed tokens, and a disallowed proposal is rejected.
+ * A position with no allowed token ends the row without a token (greedy rows:
+ * id -1).  A state id >= num_states leaves its position unmasked and sets
+ * device status bit 0.  No counterpart in the reference: its speculative paths
+ * verify without the grammar mask (docs/constrained_generation.md:243-246). */
+int32_t tg_spec_verify_masked(tg_sampler* s, const void* target_logits,
+                              const void* draft_logits, int32_t dtype, int32_t batch,
+                              int32_t K, const int32_t* draft_ids, const float* temperature,
+                              const float* u_accept, const float* u_draw,
+                              const uint32_t* mask_table, int32_t num_states,
+                              const int32_t* state_ids, int32_t* out_ids, int32_t* out_n,
+                              void* stream);
+
 /* Allocation-free variant of tg_spec_verify.  No counterpart in the reference.
  * For callers that cannot call cudaMalloc: for example a serving process that
  * reserved all free HBM for its KV cache at start-up (a cudaMalloc would fail),

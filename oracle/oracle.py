@@ -40,6 +40,8 @@ def lib():
         L.tgo_sample.restype = i32
         L.tgo_spec_verify.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
         L.tgo_spec_verify.restype = i32
+        L.tgo_spec_verify_masked.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp, vp, vp]
+        L.tgo_spec_verify_masked.restype = i32
         L.tgo_exp.argtypes = [ctypes.c_float]
         L.tgo_exp.restype = ctypes.c_float
         L.tgo_qmass.argtypes = [ctypes.c_float]
@@ -143,6 +145,26 @@ def spec_verify(target, draft, draft_ids, temperature, u_accept, u_draw):
                                _p(temperature), _p(u_accept), _p(u_draw), _p(out), _p(n))
     if rc != 0:
         raise RuntimeError(f"tgo_spec_verify failed: {rc}")
+    return out, n
+
+
+def spec_verify_masked(target, draft, draft_ids, temperature, u_accept, u_draw, mask_table, state_ids):
+    """Oracle tg_spec_verify_masked: mask_table [S, ceil(V/32)] uint32, state_ids [B, K+1]."""
+    target = np.ascontiguousarray(target)
+    B, K1, V = target.shape
+    K = K1 - 1
+    draft = np.ascontiguousarray(draft) if draft is not None else None
+    args = [np.ascontiguousarray(draft_ids, dtype=np.int32), np.ascontiguousarray(temperature, dtype=np.float32),
+            np.ascontiguousarray(u_accept, dtype=np.float32), np.ascontiguousarray(u_draw, dtype=np.float32)]
+    mask_table = np.ascontiguousarray(mask_table, dtype=np.uint32)
+    state_ids = np.ascontiguousarray(state_ids, dtype=np.int32)
+    out = np.empty((B, K + 1), np.int32)
+    n = np.empty(B, np.int32)
+    rc = lib().tgo_spec_verify_masked(_p(target), _p(draft), dtype_code(target), B, K, V,
+                                      *[_p(x) for x in args], _p(mask_table), mask_table.shape[0],
+                                      _p(state_ids), _p(out), _p(n))
+    if rc != 0:
+        raise RuntimeError(f"tgo_spec_verify_masked failed: {rc}")
     return out, n
 
 

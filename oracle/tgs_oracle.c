@@ -325,20 +325,47 @@ int32_t tgo_sample_row_detail(const void* logits, int32_t dtype, int32_t vocab,
 
 /* ---- speculative verification ------------------------------------------------ */
 
+/* Grammar-masked verification (a build-defined extension; the reference's
+ * speculative paths apply no mask, docs/constrained_generation.md:243-246 of the
+ * reference).  m: the position's mask row or NULL; a clear bit makes the element
+ * -inf in the target and the draft rows of that position. */
+static int allowed(const uint32_t* m, int32_t v) { return !m || ((m[v >> 5] >> (v & 31)) & 1u); }
+
+static const uint32_t* pos_mask(const uint32_t* table, int32_t nstates, int32_t words,
+                                const int32_t* sids, int64_t idx) {
+  if (!table || !sids) return NULL;
+  const int32_t sid = sids[idx];
+  if (sid < 0 || sid >= nstates) return NULL; /* out of range: unmasked (status bit on the GPU) */
+  return table + (int64_t)sid * words;
+}
+
 /* Masses of one tempered row: q[v] = qmass(x[v]/T - max), returns the total. */
 static uint64_t row_masses(const void* logits, int32_t dtype, int64_t base, int32_t V,
-                           float T, float* s, uint64_t* q) {
-  float m = -INFINITY;
+                           float T, float* s, uint64_t* q, const uint32_t* m) {
+  float mx = -INFINITY;
   for (int32_t v = 0; v < V; v++) {
-    s[v] = load_logit(logits, dtype, base + v) / T;
-    if (s[v] > m) m = s[v];
+    s[v] = allowed(m, v) ? load_logit(logits, dtype, base + v) / T : -INFINITY;
+    if (s[v] > mx) mx = s[v];
   }
   uint64_t Z = 0;
-  for (int32_t v = 0; v < V; v++) { q[v] = tgo_qmass(s[v] - m); Z += q[v]; }
+  for (int32_t v = 0; v < V; v++) { q[v] = tgo_qmass(s[v] - mx); Z += q[v]; }
   return Z;
 }
 
-static int32_t row_argmax(const void* logits, int32_t dtype, int64_t base, int32_t V) {
+/* First index of the maximum; with a mask, of the maximum over the allowed
+ * elements above -inf (-1 when there is none). */
+static int32_t row_argmax(const void* logits, int32_t dtype, int64_t base, int32_t V,
+                          const uint32_t* m) {
+  if (m) {
+    int32_t best = -1;
+    float bv = -INFINITY;
+    for (int32_t v = 0; v < V; v++) {
+      if (!allowed(m, v)) continue;
+      float x = load_logit(logits, dtype, base + v);
+      if (x > bv) { bv = x; best = v; }
+    }
+    return best;
+  }
   int32_t best = 0;
   float bv = load_logit(logits, dtype, base);
   for (int32_t v = 1; v < V; v++) {
@@ -348,13 +375,15 @@ static int32_t row_argmax(const void* logits, int32_t dtype, int64_t base, int32
   return best;
 }
 
-int32_t tgo_spec_verify(const void* target, const void* draft, int32_t dtype, int32_t batch,
-                        int32_t K, int32_t vocab, const int32_t* draft_ids,
-                        const float* temperature, const float* u_accept, const float* u_draw,
-                        int32_t* out_ids, int32_t* out_n) {
+static int32_t spec_verify_impl(const void* target, const void* draft, int32_t dtype, int32_t batch,
+                                int32_t K, int32_t vocab, const int32_t* draft_ids,
+                                const float* temperature, const float* u_accept, const float* u_draw,
+                                const uint32_t* mask_table, int32_t num_states, const int32_t* state_ids,
+                                int32_t* out_ids, int32_t* out_n) {
   if (!target || !draft_ids || !temperature || !out_ids || !out_n || K < 0 || vocab <= 0)
     return TG_ERR_INVALID_ARG;
   const int32_t V = vocab;
+  const int32_t W = (V + 31) / 32;
 #pragma omp parallel
   {
     float* s = (float*)malloc(sizeof(float) * (size_t)V);
@@ -370,12 +399,16 @@ int32_t tgo_spec_verify(const void* target, const void* draft, int32_t dtype, in
         /* greedy verify: SpeculativeDecode.swift:41-98 */
         int32_t i;
         for (i = 0; i < K; i++) {
-          const int32_t a = row_argmax(target, dtype, ((int64_t)b * (K + 1) + i) * V, V);
+          const uint32_t* m = pos_mask(mask_table, num_states, W, state_ids, (int64_t)b * (K + 1) + i);
+          const int32_t a = row_argmax(target, dtype, ((int64_t)b * (K + 1) + i) * V, V, m);
           const int32_t tok = draft_ids[(int64_t)b * K + i];
           if (a == tok) { out[n++] = tok; }
           else { out[n++] = a; break; }
         }
-        if (i == K) out[n++] = row_argmax(target, dtype, ((int64_t)b * (K + 1) + K) * V, V);
+        if (i == K) {
+          const uint32_t* m = pos_mask(mask_table, num_states, W, state_ids, (int64_t)b * (K + 1) + K);
+          out[n++] = row_argmax(target, dtype, ((int64_t)b * (K + 1) + K) * V, V, m);
+        }
         out_n[b] = n;
         continue;
       }
@@ -383,12 +416,13 @@ int32_t tgo_spec_verify(const void* target, const void* draft, int32_t dtype, in
       int32_t i;
       int rejected = 0;
       for (i = 0; i < K; i++) {
+        const uint32_t* m = pos_mask(mask_table, num_states, W, state_ids, (int64_t)b * (K + 1) + i);
         const int64_t tb = ((int64_t)b * (K + 1) + i) * V;
         const int64_t db = ((int64_t)b * K + i) * V;
-        const uint64_t ZT = row_masses(target, dtype, tb, V, T, s, qT);
-        const uint64_t ZD = row_masses(draft, dtype, db, V, T, s, qD);
+        const uint64_t ZT = row_masses(target, dtype, tb, V, T, s, qT, m);
+        const uint64_t ZD = row_masses(draft, dtype, db, V, T, s, qD, m);
         int32_t tok = draft_ids[(int64_t)b * K + i];
-        if (tok < 0 || tok >= V) { tok = -1; }
+        if (tok < 0 || tok >= V || !allowed(m, tok)) { tok = -1; } /* a disallowed proposal is rejected */
         double pT = tok >= 0 ? (double)qT[tok] / (double)ZT : 0.0;
         double pD = tok >= 0 ? (double)qD[tok] / (double)ZD : 0.0;
         double den = pD > 1e-10 ? pD : 1e-10;
@@ -407,18 +441,37 @@ int32_t tgo_spec_verify(const void* target, const void* draft, int32_t dtype, in
         const uint64_t* w = qD;
         uint64_t tot = R;
         if (!((double)R * (1.0 / 4503599627370496.0) > 1e-10)) { w = qT; tot = ZT; }
-        out[n++] = (int32_t)draw_index(w, V, tot, u_draw[b]);
+        if (tot > 0) out[n++] = (int32_t)draw_index(w, V, tot, u_draw[b]); /* empty: no token */
         rejected = 1;
         break;
       }
       if (!rejected) {
+        const uint32_t* m = pos_mask(mask_table, num_states, W, state_ids, (int64_t)b * (K + 1) + K);
         const int64_t tb = ((int64_t)b * (K + 1) + K) * V;
-        const uint64_t ZT = row_masses(target, dtype, tb, V, T, s, qT);
-        out[n++] = (int32_t)draw_index(qT, V, ZT, u_draw[b]);
+        const uint64_t ZT = row_masses(target, dtype, tb, V, T, s, qT, m);
+        if (ZT > 0) out[n++] = (int32_t)draw_index(qT, V, ZT, u_draw[b]);
       }
       out_n[b] = n;
     }
     free(s); free(qT); free(qD);
   }
   return TG_OK;
+}
+
+int32_t tgo_spec_verify(const void* target, const void* draft, int32_t dtype, int32_t batch,
+                        int32_t K, int32_t vocab, const int32_t* draft_ids,
+                        const float* temperature, const float* u_accept, const float* u_draw,
+                        int32_t* out_ids, int32_t* out_n) {
+  return spec_verify_impl(target, draft, dtype, batch, K, vocab, draft_ids, temperature, u_accept,
+                          u_draw, NULL, 0, NULL, out_ids, out_n);
+}
+
+/* state_ids [batch, K+1]: the grammar state before each position's token (-1: unmasked). */
+int32_t tgo_spec_verify_masked(const void* target, const void* draft, int32_t dtype, int32_t batch,
+                               int32_t K, int32_t vocab, const int32_t* draft_ids,
+                               const float* temperature, const float* u_accept, const float* u_draw,
+                               const uint32_t* mask_table, int32_t num_states, const int32_t* state_ids,
+                               int32_t* out_ids, int32_t* out_n) {
+  return spec_verify_impl(target, draft, dtype, batch, K, vocab, draft_ids, temperature, u_accept,
+                          u_draw, mask_table, num_states, state_ids, out_ids, out_n);
 }

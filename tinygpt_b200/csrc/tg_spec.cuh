@@ -57,7 +57,26 @@ struct SpecArgs {
   // the rejecting position, or -2 when the row is finished (greedy)
   int32_t* rstate;  // nullptr: eager (every position at once)
   int32_t lazy_pos; // position of this lazy stats launch (K: the bonus row)
+  // grammar masks (tg_spec_verify_masked): state_ids [batch, K+1], the state
+  // before each position's token (-1: unmasked); nullptr: no masks
+  const uint32_t* mask_table;
+  int32_t num_states;
+  int32_t mask_words;
+  const int32_t* state_ids;
 };
+
+// Mask row of position i of batch row b (nullptr: unmasked).  An out-of-range
+// state leaves the position unmasked and sets status bit 0.
+__device__ __forceinline__ const uint32_t* spec_mask(const SpecArgs& a, int b, int i) {
+  if (!a.state_ids) return nullptr;
+  const int sid = a.state_ids[static_cast<int64_t>(b) * (a.K + 1) + i];
+  if (sid < 0) return nullptr;
+  if (sid >= a.num_states) {
+    atomicOr(a.status, 1u);
+    return nullptr;
+  }
+  return a.mask_table + static_cast<int64_t>(sid) * a.mask_words;
+}
 
 __device__ __forceinline__ float spec_T(float t0) { return fmaxf(t0, 1e-5f); }
 
@@ -152,6 +171,12 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     row = reinterpret_cast<const char*>(a.draft) + (static_cast<int64_t>(b) * a.K + (pos - a.K - 1)) * V * E::kSize;
   }
   const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
+  const uint32_t* msk = spec_mask(a, b, pos <= a.K ? pos : pos - a.K - 1);
+  // element i of the slice, -inf where the position's mask clears it
+  auto elem = [&](int i) {
+    const float x = smem_elem<DT>(slice, i);
+    return (msk && !mask_allows(msk, c0 + i)) ? neg_inf() : x;
+  };
   if (t == 0) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bar)) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -166,7 +191,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   int id = 0x7fffffff;
   if (ok) {
     for (int i = t; i < c1 - c0; i += kSpecNT) {
-      const float x = smem_elem<DT>(slice, i);
+      const float x = elem(i);
       if (x > y) { y = x; id = c0 + i; }
     }
   }
@@ -178,6 +203,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     const int oi = *cluster.map_shared_rank(&c_arg, q);
     if (q == 0 || oy > y || (oy == y && oi < id)) { y = oy; id = oi; }
   }
+  if (msk && id == 0x7fffffff) id = -1;  // nothing allowed above -inf
   if (greedy) {
     if (rank == 0 && t == 0) a.stats[r] = SpecStat{y, id, 0ull};
     cluster.sync();  // peers still read this CTA's maximum
@@ -188,7 +214,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   unsigned long long Z = 0;
   if (ok) {
     for (int i = t; i < c1 - c0; i += kSpecNT)
-      Z += qmass(__fsub_rn(__fdiv_rn(smem_elem<DT>(slice, i), T), smax));
+      Z += qmass(__fsub_rn(__fdiv_rn(elem(i), T), smax));
   }
   Z = block_sum<kSpecNT>(Z, sm);
   if (t == 0) c_z = Z;
@@ -229,7 +255,10 @@ __device__ __forceinline__ void spec_accept_step(const SpecArgs& a, int b, int i
     return;
   }
   bool accept = false;
-  if (tok >= 0 && tok < V) {
+  const uint32_t* msk = spec_mask(a, b, i);
+  if (tok >= 0 && tok < V && msk && !mask_allows(msk, tok)) {
+    // a proposal the grammar does not allow is rejected
+  } else if (tok >= 0 && tok < V) {
     const char* trow = reinterpret_cast<const char*>(a.target) + (static_cast<int64_t>(b) * (K + 1) + i) * V * E::kSize;
     const char* drow = reinterpret_cast<const char*>(a.draft) + (static_cast<int64_t>(b) * K + i) * V * E::kSize;
     const unsigned long long qT = qmass(__fsub_rn(__fdiv_rn(E::load(trow, tok), T), st[i].smax));
@@ -324,16 +353,18 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
   const int sub = (c1 - c0 + kSpecNT - 1) / kSpecNT;
   const int v0 = min(c1, c0 + t * sub), v1 = min(c1, v0 + sub);
-  auto qt_of = [&](int v) { return qmass(__fsub_rn(__fdiv_rn(E::load(trow, v), T), smT)); };
+  const uint32_t* msk = spec_mask(a, b, pos);
+  auto ld = [&](const char* row, int v) { return (msk && !mask_allows(msk, v)) ? neg_inf() : E::load(row, v); };
+  auto qt_of = [&](int v) { return qmass(__fsub_rn(__fdiv_rn(ld(trow, v), T), smT)); };
   auto rq_of = [&](int v) {
-    const unsigned long long qd = qmass(__fsub_rn(__fdiv_rn(E::load(drow, v), T), smD));
+    const unsigned long long qd = qmass(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
     return resid_mass(qt_of(v), ZT, qd, ZD);
   };
   unsigned long long sT = 0, sR = 0;
   if (fin >= 0) {
     for (int v = v0; v < v1; v++) {
       const unsigned long long qt = qt_of(v);
-      const unsigned long long qd = qmass(__fsub_rn(__fdiv_rn(E::load(drow, v), T), smD));
+      const unsigned long long qd = qmass(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
       sT += qt;
       sR += resid_mass(qt, ZT, qd, ZD);
     }
@@ -358,6 +389,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const unsigned long long mine = use_resid ? sR : sT;
   const unsigned long long before = (use_resid ? preR + befR : preT + befT);
   const unsigned long long rpt = draw_point(a.u_draw[b], total);
+  if (total == 0 && rank == 0 && t == 0) a.out_n[b] = n0;  // masked away entirely: no token
   if (mine > 0 && before <= rpt && rpt < before + mine) {
     unsigned long long c = before;
     int pick = v1 - 1;

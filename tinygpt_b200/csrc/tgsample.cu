@@ -411,11 +411,14 @@ int32_t tg_sample_host(tg_sampler* s, const void* logits, int32_t dtype, int64_t
   return TG_OK;
 }
 
-int32_t tg_spec_verify(tg_sampler* s, const void* target_logits, const void* draft_logits,
-                       int32_t dtype, int32_t batch, int32_t K, const int32_t* draft_ids,
-                       const float* temperature, const float* u_accept, const float* u_draw,
-                       int32_t* out_ids, int32_t* out_n, void* stream) {
+static int32_t spec_verify_impl(tg_sampler* s, const void* target_logits, const void* draft_logits,
+                                int32_t dtype, int32_t batch, int32_t K, const int32_t* draft_ids,
+                                const float* temperature, const float* u_accept, const float* u_draw,
+                                const uint32_t* mask_table, int32_t num_states, const int32_t* state_ids,
+                                int32_t* out_ids, int32_t* out_n, void* stream) {
   if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (state_ids && (!mask_table || num_states <= 0))
+    return fail(TG_ERR_INVALID_ARG, "state_ids given without mask_table / num_states");
   if (dtype != TG_DTYPE_F32 && dtype != TG_DTYPE_BF16) return fail(TG_ERR_INVALID_ARG, "bad dtype");
   if (batch < 0 || batch > s->max_batch) return fail(TG_ERR_INVALID_ARG, "batch outside [0, max_batch]");
   if (K < 0 || K > 64) return fail(TG_ERR_UNSUPPORTED, "K outside [0, 64]");
@@ -432,11 +435,35 @@ int32_t tg_spec_verify(tg_sampler* s, const void* target_logits, const void* dra
                  u_accept, u_draw, out_ids, out_n, static_cast<tg::SpecStat*>(s->stats.p),
                  s->d_status};
   a.rstate = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(s->stats.p) + nst);
+  if (state_ids) {
+    a.mask_table = mask_table;
+    a.num_states = num_states;
+    a.mask_words = (s->vocab + 31) / 32;
+    a.state_ids = state_ids;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaError_t le = dtype == TG_DTYPE_F32 ? tg::launch_spec<0>(a, st) : tg::launch_spec<1>(a, st);
   if (le == cudaErrorInvalidValue) return fail(TG_ERR_UNSUPPORTED, "vocab too large for the staged verification (vocab * element size > 1.6 MB)");
   TG_CUDA(le);
   return TG_OK;
+}
+
+int32_t tg_spec_verify(tg_sampler* s, const void* target_logits, const void* draft_logits,
+                       int32_t dtype, int32_t batch, int32_t K, const int32_t* draft_ids,
+                       const float* temperature, const float* u_accept, const float* u_draw,
+                       int32_t* out_ids, int32_t* out_n, void* stream) {
+  return spec_verify_impl(s, target_logits, draft_logits, dtype, batch, K, draft_ids, temperature,
+                          u_accept, u_draw, nullptr, 0, nullptr, out_ids, out_n, stream);
+}
+
+int32_t tg_spec_verify_masked(tg_sampler* s, const void* target_logits, const void* draft_logits,
+                              int32_t dtype, int32_t batch, int32_t K, const int32_t* draft_ids,
+                              const float* temperature, const float* u_accept, const float* u_draw,
+                              const uint32_t* mask_table, int32_t num_states, const int32_t* state_ids,
+                              int32_t* out_ids, int32_t* out_n, void* stream) {
+  if (!state_ids) return fail(TG_ERR_INVALID_ARG, "state_ids is required");
+  return spec_verify_impl(s, target_logits, draft_logits, dtype, batch, K, draft_ids, temperature,
+                          u_accept, u_draw, mask_table, num_states, state_ids, out_ids, out_n, stream);
 }
 
 int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_logits,

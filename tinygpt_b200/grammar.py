@@ -174,3 +174,22 @@ class MaskTableBatch:
     def commit(self, ids) -> list[bool]:
         ids = np.asarray(ids.cpu() if hasattr(ids, "cpu") else ids).reshape(-1)
         return [s.commit(int(t)) for s, t in zip(self.states, ids)]
+
+
+def draft_state_rows(states, draft_ids) -> np.ndarray:
+    """State rows [B, K+1] for tg_spec_verify_masked: entry i is the mask-table
+    row of the grammar state before draft token i of the row (state after
+    tokens 0..i-1, computed on a clone; the live states are not advanced).
+    After a proposal the grammar rejects, the later positions keep the state
+    before it (verification stops at that proposal anyway)."""
+    draft_ids = np.asarray(draft_ids.cpu() if hasattr(draft_ids, "cpu") else draft_ids)
+    B, K = draft_ids.shape
+    rows = np.empty((B, K + 1), np.int32)
+    for b, st in enumerate(states):
+        c = st.clone()
+        ok = True
+        for i in range(K + 1):
+            rows[b, i] = c.row()
+            if i < K and ok:
+                ok = c.commit(int(draft_ids[b, i]))
+    return rows

@@ -166,6 +166,25 @@ class Sampler:
                                      _ptr(out_n), _stream_ptr(stream)))
         return out, out_n
 
+    def spec_verify_masked(self, target_logits, draft_logits, draft_ids, temperature, u_accept,
+                           u_draw, mask_table, state_ids, *, out=None, out_n=None, stream=None):
+        """tg_spec_verify_masked: mask_table int32/uint32 [S, ceil(V/32)] and
+        state_ids int32 [B, K+1] device tensors (the grammar state before each
+        position's token)."""
+        B, K1, V = target_logits.shape
+        K = K1 - 1
+        dev = target_logits.device
+        if out is None:
+            out = torch.empty((B, K + 1), dtype=torch.int32, device=dev)
+        if out_n is None:
+            out_n = torch.empty(B, dtype=torch.int32, device=dev)
+        check(self._L.tg_spec_verify_masked(self._h, _ptr(target_logits), _ptr(draft_logits),
+                                            _dtype_code(target_logits), B, K, _ptr(draft_ids),
+                                            _ptr(temperature), _ptr(u_accept), _ptr(u_draw),
+                                            _ptr(mask_table), mask_table.shape[0], _ptr(state_ids),
+                                            _ptr(out), _ptr(out_n), _stream_ptr(stream)))
+        return out, out_n
+
     def sample_shard_local(self, logits, params, vocab_offset: int, full_vocab: int, *,
                            history=None, history_len=None, mask_table=None, state_id=None,
                            out_records=None, stream=None):
