@@ -60,6 +60,12 @@ constexpr float kTgtMul = 1.5f;
 constexpr float kTgtAdd = 96.0f;
 constexpr int kRing = 64;  // hit-vector ring entries per warp (drained at 32)
 static_assert((kSampleNT / 32) * kRing * 20 <= kCandMax * 4, "rings must fit in cand_e");
+constexpr int kWideNT = 1024;  // threads per CTA for small batches
+// Batches of kWideMinBatch..kWideMaxBatch rows run on wide CTAs (measured: a
+// 1024-thread CTA makes 64 rows without top-k 2.3x faster; a single top-k row is
+// faster on 256 threads).
+constexpr int kWideMinBatch = 8;
+constexpr int kWideMaxBatch = 148;
 static_assert(kCandMax <= kWideMassN, "candidate mass histograms must not overflow their limbs");
 
 // Diagnostic build only (-DTG_PHASE_TIMING): cycles per phase summed over CTAs.
@@ -143,7 +149,7 @@ struct Hist {
 
 // Every element of the row, recomputed from global memory (L2 after the first
 // pass): 128-bit loads over the aligned middle, scalars for head and tail.
-template <int DT>
+template <int DT, int NT = kSampleNT>
 struct GlobalSrc {
   const char* row;
   int V, head, nvec, tail0;
@@ -163,7 +169,7 @@ struct GlobalSrc {
     if (t < head) one(t, E::load(row, t));
     if (t < V - tail0) one(tail0 + t, E::load(row, tail0 + t));
     const uint4* vrow = reinterpret_cast<const uint4*>(row + head * E::kSize);
-    for (int j = t; j < nvec; j += kSampleNT) {
+    for (int j = t; j < nvec; j += NT) {
       float x[EPV];
       E::unpack(__ldg(vrow + j), x);
       const int e0 = head + j * EPV;
@@ -178,14 +184,15 @@ struct GlobalSrc {
   }
 };
 
-struct SmemSrc {
+template <int NT = kSampleNT>
+struct SmemSrcT {
   const float* y;
   const int* id;
   int n;
   float theta;
   template <class F>
   __device__ __forceinline__ void for_each(F&& f) const {
-    for (int i = threadIdx.x; i < n; i += kSampleNT) {
+    for (int i = threadIdx.x; i < n; i += NT) {
       const float v = y[i];
       const int d = id[i];
       if (d >= 0 && v >= theta) f(d, v);
@@ -203,17 +210,17 @@ struct RegSrc {  // N values per thread, held in registers
   }
 };
 
-template <class Src>
+template <int NT = kSampleNT, class Src>
 __device__ __forceinline__ unsigned int block_count_if(const Src& src, float thr, BlockScratch& sm) {
   unsigned long long c = 0;
   src.for_each([&](int, float y) { c += (y >= thr) ? 1ull : 0ull; });
-  return static_cast<unsigned int>(block_sum<kSampleNT>(c, sm));
+  return static_cast<unsigned int>(block_sum<NT>(c, sm));
 }
 
 // Stages (b)-(e) over a source.  Returns false (and writes nothing) when the
 // source is a candidate list that turns out to miss an element the top-k
 // threshold keeps; the caller then reruns the row over the full row.
-template <class Src>
+template <int NT = kSampleNT, class Src>
 __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float u,
                            bool check_theta, float theta, BlockScratch& sm, int& out_id,
                            float& out_prob) {
@@ -223,7 +230,7 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
     src.for_each([&](int i, float v) {
       if (v > y || (v == y && i < id)) { y = v; id = i; }
     });
-    block_argmax<kSampleNT>(y, id, sm);
+    block_argmax<NT>(y, id, sm);
     if (y == neg_inf()) { out_id = -1; out_prob = 0.0f; }
     else { out_id = id; out_prob = 1.0f; }
     return true;
@@ -234,7 +241,7 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
   if (topk) {
     uint32_t kkey; unsigned long long b0, m0; unsigned int c0, n0;
     const unsigned int k = static_cast<unsigned int>(p.top_k);
-    radix_find<kSampleNT, true, false>(
+    radix_find<NT, true, false>(
         src, 32,
         [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; },
         [&](unsigned long long, unsigned int c) { return c >= k; }, sm, kkey, b0, c0, n0, m0);
@@ -248,7 +255,7 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
   }
   float ymax = neg_inf();
   src.for_each([&](int, float y) { ymax = fmaxf(ymax, y); });
-  ymax = block_max<kSampleNT>(ymax, sm);
+  ymax = block_max<NT>(ymax, sm);
   if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
   const float smax = __fdiv_rn(ymax, T);
 
@@ -263,7 +270,7 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
     float s;
     if (inA(y, s)) Q += qmass(__fsub_rn(s, smax));
   });
-  Q = block_sum<kSampleNT>(Q, sm);
+  Q = block_sum<NT>(Q, sm);
 
   // (d) top-p: last element (cut_key, cut_id) of the shortest (s desc, id asc)
   // prefix whose mass reaches top_p * Q.
@@ -282,10 +289,10 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
         float s;
         if (inA(y, s) && fkey(s) == cut_key) c++;
       });
-      nties = static_cast<unsigned int>(block_sum<kSampleNT>(c, sm));
+      nties = static_cast<unsigned int>(block_sum<NT>(c, sm));
     } else {
       unsigned int cb;
-      radix_find<kSampleNT, true, true>(
+      radix_find<NT, true, true>(
           src, 32,
           [&](int, float y, uint32_t& key, unsigned long long& w) {
             float s;
@@ -311,7 +318,7 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
     if (jstar < nties) {
       uint32_t idkey; unsigned long long b1, m1; unsigned int c1, n1;
       const unsigned int js = static_cast<unsigned int>(jstar);
-      radix_find<kSampleNT, false, false>(
+      radix_find<NT, false, false>(
           src, 20,
           [&](int id, float y, uint32_t& key, unsigned long long& w) {
             float s;
@@ -343,11 +350,11 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
     unsigned long long q;
     if (inF(id, y, q)) S += q;
   });
-  S = block_sum<kSampleNT>(S, sm);
+  S = block_sum<NT>(S, sm);
   const unsigned long long r = draw_point(u, S);
 
   uint32_t pick; unsigned long long b2, qpick; unsigned int c2, n2;
-  radix_find<kSampleNT, false, true>(
+  radix_find<NT, false, true>(
       src, 20,
       [&](int id, float y, uint32_t& key, unsigned long long& w) {
         if (!inF(id, y, w)) return false;
@@ -363,13 +370,14 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
 // Survivors of the candidate path after compaction: slot i holds the tempered
 // logit s (cand_y), the id (cand_id, -1 when dropped) and e = tg_exp(s - smax)
 // (cand_e), so q = trunc(e * 2^44) needs no division or exponential.
-struct ASrc {
+template <int NT = kSampleNT>
+struct ASrcT {
   const float* s;
   const int* id;
   int n;
   template <class F>
   __device__ __forceinline__ void for_each(F&& f) const {
-    for (int i = threadIdx.x; i < n; i += kSampleNT)
+    for (int i = threadIdx.x; i < n; i += NT)
       if (id[i] >= 0) f(i, s[i]);
   }
 };
@@ -387,13 +395,14 @@ __device__ __forceinline__ unsigned long long mass_of_e(float e) {
 // q_rest is then the exact mass of every other finite element.  The row can be
 // finished from the list when the top-p cut falls inside it, or when min-p
 // provably drops everything below theta; otherwise false.
+template <int NT = kSampleNT>
 __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
                              const tg_row_params& p, int V, float u, BlockScratch& sm,
                              int& out_id, float& out_prob, PhaseClock& pc, bool partial = false,
                              unsigned long long q_rest = 0, float below_override = 0.0f,
                              bool use_below = false) {
-  SmemSrc src{cy, cid, n, theta};
-  if (!(p.temperature > 0.0f)) return finish_row(src, p, V, u, false, theta, sm, out_id, out_prob);
+  SmemSrcT<NT> src{cy, cid, n, theta};
+  if (!(p.temperature > 0.0f)) return finish_row<NT>(src, p, V, u, false, theta, sm, out_id, out_prob);
   const float T = p.temperature;
   const bool topk = p.top_k > 0 && p.top_k < V;
   const int lane = threadIdx.x & 31;
@@ -403,7 +412,7 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
     ymax = fmaxf(ymax, y);
     if (y > neg_inf()) nymin = fmaxf(nymin, -y);
   });
-  block_max2<kSampleNT>(ymax, nymin, sm);
+  block_max2<NT>(ymax, nymin, sm);
   const float ymin = -nymin;
   if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return !partial; }
   // an upper bound of the values absent from the list
@@ -421,12 +430,12 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       const int bn = static_cast<int>(__fmul_rn(__fsub_rn(ymax, y), scale));
       return bn > 2046 ? 2046 : bn;
     };
-    const HistSel hs = hist_round<kSampleNT, 2048, false>(
+    const HistSel hs = hist_round<NT, 2048, false>(
         src, [&](int, float y, int& bin, unsigned long long& w) { bin = binf(y); w = 1; return true; },
         [&](unsigned long long c) { return c >= k; }, sm);
     if (hs.bin < 0) return false;
     const unsigned int j = k - static_cast<unsigned int>(hs.before);  // rank inside the bin
-    const int nb = collect_small<kSampleNT>(
+    const int nb = collect_small<NT>(
         src,
         [&](int i, float y, unsigned long long& key, unsigned long long& w, int& id) {
           if (binf(y) != hs.bin) return false;
@@ -452,8 +461,8 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       src.for_each([&](int, float y) {
         if (binf(y) == hs.bin) { lo = max(lo, ~fkey(y)); hi = max(hi, fkey(y)); }
       });
-      lo = ~block_max_u32<kSampleNT>(lo, sm);
-      hi = block_max_u32<kSampleNT>(hi, sm);
+      lo = ~block_max_u32<NT>(lo, sm);
+      hi = block_max_u32<NT>(hi, sm);
       if (lo == hi) {
         kkey = hi;
       } else {
@@ -463,7 +472,7 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
           key = fkey(y); w = 0; return true;
         };
         auto rc = [&](unsigned long long, unsigned int c) { return c >= j; };
-        radix_find<kSampleNT, true, false, SmemSrc, decltype(kw), decltype(rc), true>(
+        radix_find<NT, true, false, SmemSrcT<NT>, decltype(kw), decltype(rc), true>(
             src, 32, kw, rc, sm, kkey, b0, c0, n0, m0);
       }
     }
@@ -488,10 +497,10 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
     const int bn = static_cast<int>(__fmul_rn(__fsub_rn(smax, sv), 32.0f));
     return bn > 1023 ? 1023 : bn;
   };
-  if (toppon) hist_zero<kSampleNT, 1024, true>(sm);
+  if (toppon) hist_zero<NT, 1024, true>(sm);
   __syncthreads();
   unsigned long long Q = 0;
-  for (int i = threadIdx.x; i < n; i += kSampleNT) {
+  for (int i = threadIdx.x; i < n; i += NT) {
     const float y = cy[i];
     bool keep = cid[i] >= 0 && y >= theta && y > neg_inf();
     float sv = 0.0f, e = 0.0f;
@@ -511,8 +520,8 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       cid[i] = -1;
     }
   }
-  Q = block_sum<kSampleNT>(Q, sm) + q_rest;
-  ASrc as{cy, cid, n};
+  Q = block_sum<NT>(Q, sm) + q_rest;
+  ASrcT<NT> as{cy, cid, n};
   pc.mark(6);
 
   // (d) top-p: the last element (cut_key, cut_id) of the shortest prefix in
@@ -523,10 +532,10 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
     const double tau = __dmul_rn(static_cast<double>(p.top_p), __ull2double_rn(Q));
     bool resolved = false;
     if (tau > 0.0) {
-      const HistSel hs = hist_scan<kSampleNT, 1024, true>(
+      const HistSel hs = hist_scan<NT, 1024, true>(
           [&](unsigned long long m) { return __ull2double_rn(m) >= tau; }, sm);
       if (hs.bin >= 0) {
-        const int nb = collect_small<kSampleNT>(
+        const int nb = collect_small<NT>(
             as,
             [&](int i, float sv, unsigned long long& key, unsigned long long& w, int& id) {
               w = mass_of_e(ce[i]);
@@ -562,14 +571,14 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       as.for_each([&](int i, float sv) {
         if (fkey(sv) == cut_key) best = max(best, ~static_cast<uint32_t>(cid[i]));
       });
-      cut_id = static_cast<int>(~block_max_u32<kSampleNT>(best, sm));
+      cut_id = static_cast<int>(~block_max_u32<NT>(best, sm));
       resolved = true;
     }
     if (!resolved) {  // crowded bin: exact radix over the whole survivor set
       unsigned long long above = 0, qt = 0;
       unsigned int nties = 0, cb;
       unsigned long long jstar = 1;
-      radix_find<kSampleNT, true, true>(
+      radix_find<NT, true, true>(
           as, 32,
           [&](int i, float sv, uint32_t& key, unsigned long long& w) {
             key = fkey(sv);
@@ -592,7 +601,7 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       if (jstar < nties) {
         uint32_t idkey; unsigned long long b1, m1; unsigned int c1, n1;
         const unsigned int js = static_cast<unsigned int>(jstar);
-        radix_find<kSampleNT, false, false>(
+        radix_find<NT, false, false>(
             as, 20,
             [&](int i, float sv, uint32_t& key, unsigned long long& w) {
               if (fkey(sv) != cut_key) return false;
@@ -608,10 +617,10 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
   pc.mark(7);
   const int idbits = 32 - __clz(V > 1 ? V - 1 : 1);
   const int shift = idbits > 10 ? idbits - 10 : 0;
-  hist_zero<kSampleNT, 1024, true>(sm);
+  hist_zero<NT, 1024, true>(sm);
   __syncthreads();
   unsigned long long S = 0;  // the same pass fills the draw histogram over id bins
-  for (int i = threadIdx.x; i < n; i += kSampleNT) {
+  for (int i = threadIdx.x; i < n; i += NT) {
     const int id = cid[i];
     if (id < 0) continue;
     const unsigned long long q = mass_of_e(ce[i]);
@@ -628,16 +637,16 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
       cid[i] = -1;
     }
   }
-  S = block_sum<kSampleNT>(S, sm);
+  S = block_sum<NT>(S, sm);
   pc.mark(8);
 
   // (e) draw: first id in index order whose running mass exceeds r
   const unsigned long long r = draw_point(u, S);
-  const HistSel hd = hist_scan<kSampleNT, 1024, true>([&](unsigned long long m) { return m > r; }, sm);
+  const HistSel hd = hist_scan<NT, 1024, true>([&](unsigned long long m) { return m > r; }, sm);
   int pick = -1;
   unsigned long long qpick = 0;
   if (hd.bin >= 0) {
-    const int nb = collect_small<kSampleNT>(
+    const int nb = collect_small<NT>(
         as,
         [&](int i, float, unsigned long long& key, unsigned long long& w, int& id) {
           w = mass_of_e(ce[i]);
@@ -662,7 +671,7 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
   }
   if (pick < 0) {
     uint32_t pk; unsigned long long b2, qp; unsigned int c2, n2;
-    radix_find<kSampleNT, false, true>(
+    radix_find<NT, false, true>(
         as, 20,
         [&](int i, float, uint32_t& key, unsigned long long& w) {
           key = static_cast<uint32_t>(cid[i]);
@@ -683,7 +692,7 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
 // bins of equal width between the largest and the smallest finite maximum,
 // then the smallest maximum inside the bin that holds the rk-th largest (a
 // lower bound of the rk-th largest; -inf when rk exceeds the sample).
-template <int N>
+template <int N, int NT = kSampleNT>
 __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm) {
   float mx = neg_inf(), nmn = neg_inf();
 #pragma unroll
@@ -691,7 +700,7 @@ __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm
     mx = fmaxf(mx, vm[i]);
     if (vm[i] > neg_inf()) nmn = fmaxf(nmn, -vm[i]);
   }
-  block_max2<kSampleNT>(mx, nmn, sm);
+  block_max2<NT>(mx, nmn, sm);
   const float mn = -nmn;
   if (mx == neg_inf()) return neg_inf();
   const float width = __fsub_rn(mx, mn);
@@ -701,7 +710,7 @@ __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm
     const int bn = static_cast<int>(__fmul_rn(__fsub_rn(mx, v), scale));
     return bn > 2046 ? 2046 : bn;
   };
-  const HistSel hs = hist_round<kSampleNT, 2048, false>(
+  const HistSel hs = hist_round<NT, 2048, false>(
       RegSrc<N>{vm}, [&](int, float v, int& bin, unsigned long long& w) { bin = binf(v); w = 1; return true; },
       [&](unsigned long long c) { return c >= rk; }, sm);
   if (hs.bin < 0 || hs.bin == 2047) return neg_inf();
@@ -709,7 +718,7 @@ __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm
 #pragma unroll
   for (int i = 0; i < N; i++)
     if (binf(vm[i]) == hs.bin) nlo = fmaxf(nlo, -vm[i]);
-  return -block_max<kSampleNT>(nlo, sm);
+  return -block_max<NT>(nlo, sm);
 }
 
 // Vocab-sharded mode, local half: the record of one row -- every local value
@@ -717,7 +726,7 @@ __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm
 // with global ids.  Rows that are neither greedy nor top-k <= kFastMaxK get
 // count -1.
 // `below`: an upper bound of the local values the source does not yield.
-template <class Src>
+template <int NT = kSampleNT, class Src>
 __device__ void shard_emit(const Src& src, const tg_row_params& p, int V, int moff,
                            tg_shard_record* rec, BlockScratch& sm, float below) {
   const int t = threadIdx.x;
@@ -728,7 +737,7 @@ __device__ void shard_emit(const Src& src, const tg_row_params& p, int V, int mo
     src.for_each([&](int i, float v) {
       if (v > y || (v == y && i < id)) { y = v; id = i; }
     });
-    block_argmax<kSampleNT>(y, id, sm);
+    block_argmax<NT>(y, id, sm);
     if (t == 0) {
       rec->flags = 0;
       rec->absent_max = neg_inf();
@@ -747,7 +756,7 @@ __device__ void shard_emit(const Src& src, const tg_row_params& p, int V, int mo
     const unsigned int k = static_cast<unsigned int>(p.top_k);
     auto kw = [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; };
     auto rc = [&](unsigned long long, unsigned int c) { return c >= k; };
-    radix_find<kSampleNT, true, false, Src, decltype(kw), decltype(rc), true>(src, 32, kw, rc, sm, kkey, b0, c0, n0, m0);
+    radix_find<NT, true, false, Src, decltype(kw), decltype(rc), true>(src, 32, kw, rc, sm, kkey, b0, c0, n0, m0);
     kth = key2f(kkey);
   }
   if (t == 0) sm.sn = 0;
@@ -761,7 +770,7 @@ __device__ void shard_emit(const Src& src, const tg_row_params& p, int V, int mo
       absent = fmaxf(absent, y);
     }
   });
-  absent = block_max<kSampleNT>(absent, sm);
+  absent = block_max<NT>(absent, sm);
   if (t == 0) {
     const int c = sm.sn;
     rec->count = c < TG_SHARD_CAP ? c : TG_SHARD_CAP;
@@ -773,8 +782,8 @@ __device__ void shard_emit(const Src& src, const tg_row_params& p, int V, int mo
 
 // kStream: the streaming half of the two-kernel mode (threshold, streaming
 // pass, raw candidates to global memory); no history, no selection code.
-template <int DT, bool kStream = false>
-__global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCtasPerSm) sample_kernel(SampleArgs a) {
+template <int DT, bool kStream = false, int NT = kSampleNT>
+__global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerSm * kSampleNT / NT > 0 ? kMinCtasPerSm * kSampleNT / NT : 1)) sample_kernel(SampleArgs a) {
   using E = Elt<DT>;
   constexpr int EPV = E::kEPV;
   constexpr int SV = kSampleVecs;
@@ -868,11 +877,11 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
   // the candidate list is penalised from its own raw values.
   auto build_hist = [&](float th, bool values) {
     if (!need_hist || hist.active) return;
-    for (int i = t; i < ht; i += kSampleNT) { hkey[i] = -1; hval[i] = 0; }
-    for (int i = t; i < 128; i += kSampleNT) bloom[i] = 0u;
+    for (int i = t; i < ht; i += NT) { hkey[i] = -1; hval[i] = 0; }
+    for (int i = t; i < 128; i += NT) bloom[i] = 0u;
     __syncthreads();
     const int32_t* h = a.history + static_cast<int64_t>(b) * a.history_stride;
-    for (int i = t; i < hlen; i += kSampleNT) {
+    for (int i = t; i < hlen; i += NT) {
       const int id = h[i] - moff;  // history ids are global
       if (id < 0 || id >= V) continue;
       int s = hist.slot0(id);
@@ -883,7 +892,7 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
       }
     }
     __syncthreads();
-    for (int s = t; s < ht; s += kSampleNT) {
+    for (int s = t; s < ht; s += NT) {
       const int id = hkey[s];
       if (id < 0) continue;
       const uint32_t hb = (static_cast<uint32_t>(id) * 0x85EBCA77u) >> 20;
@@ -972,8 +981,12 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
     // Per-warp ring of hit vectors (raw 16 bytes + vector index) in the bytes
     // of cand_e, which stage (b) only needs later.  A warp drains its ring
     // itself whenever it holds >= 32 entries: lane i expands entries i, i+32.
-    uint4* rdata = reinterpret_cast<uint4*>(cand_e) + warp * kRing;
-    int* ridx = reinterpret_cast<int*>(reinterpret_cast<uint4*>(cand_e) + (kSampleNT / 32) * kRing) + warp * kRing;
+    // (wide CTAs: the rings get their own shared memory after the hash)
+    uint4* rbase = reinterpret_cast<uint4*>(cand_e);
+    if constexpr (!kStream && (NT / 32) * kRing * 20 > kCandMax * 4)
+      rbase = reinterpret_cast<uint4*>(dyn + kCandMax * 12 + (ht ? static_cast<size_t>(8) * ht : 0));
+    uint4* rdata = rbase + warp * kRing;
+    int* ridx = reinterpret_cast<int*>(rbase + (NT / 32) * kRing) + warp * kRing;
     auto drain = [&](int cnt, float th) {  // warp-uniform cnt <= kRing
       __syncwarp();
       for (int i0 = 0; i0 < cnt; i0 += 32) {
@@ -1017,8 +1030,8 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
       auto group = [&](const uint4* w, int jb) {
 #pragma unroll
         for (int q = 0; q < kUnroll; q++) {
-          if (jb + q * kSampleNT >= nvec) break;  // warp-uniform
-          const int j = jb + q * kSampleNT + t;
+          if (jb + q * NT >= nvec) break;  // warp-uniform
+          const int j = jb + q * NT + t;
           const bool hit = j < nvec && vmax_of(w[q], j) >= th;
           const unsigned bal = __ballot_sync(kFull, hit);
           if (bal) {
@@ -1036,19 +1049,19 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
       if (!mask) {
         // full groups: no bounds checks, and one packed max over the lane's
         // vectors decides whether the warp needs the exact per-vector test
-        for (; jb + kUnroll * kSampleNT <= nvec; jb += kUnroll * kSampleNT) {
+        for (; jb + kUnroll * NT <= nvec; jb += kUnroll * NT) {
           const uint4* pv = vrow + jb + t;
           uint4 w[kUnroll];
 #pragma unroll
-          for (int q = 0; q < kUnroll; q++) w[q] = ldg_stream(pv + q * kSampleNT);
+          for (int q = 0; q < kUnroll; q++) w[q] = ldg_stream(pv + q * NT);
           if (__any_sync(kFull, E::template vmax_n<kUnroll>(w) >= th)) group(w, jb);
         }
       }
-      for (; jb < nvec; jb += kUnroll * kSampleNT) {
+      for (; jb < nvec; jb += kUnroll * NT) {
         uint4 w[kUnroll];
 #pragma unroll
         for (int q = 0; q < kUnroll; q++) {
-          const int j = jb + q * kSampleNT + t;
+          const int j = jb + q * NT + t;
           if (j < nvec) w[q] = ldg_stream(vrow + j);
         }
         group(w, jb);
@@ -1062,7 +1075,7 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
 
     // Sample: the first SV vectors of every thread; their per-vector maxima
     // give the threshold for the rest of the row.
-    const int nsv = nvec < SV * kSampleNT ? nvec : SV * kSampleNT;
+    const int nsv = nvec < SV * NT ? nvec : SV * NT;
     const int sampled = nsv * EPV;
     auto rank_for = [&](float mult) {
       int rr = static_cast<int>(ceilf(mult * tgt * static_cast<float>(sampled > 0 ? sampled : 1) /
@@ -1081,7 +1094,7 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
       const int m = n < kCandMax ? n : kCandMax;
       const float* gy = a.cand_gy + static_cast<int64_t>(b) * kCandMax;
       const int* gid = a.cand_gid + static_cast<int64_t>(b) * kCandMax;
-      for (int i = t; i < m; i += kSampleNT) {
+      for (int i = t; i < m; i += NT) {
         cand_y[i] = __ldcs(gy + i);
         cand_id[i] = __ldcs(gid + i);
       }
@@ -1095,30 +1108,30 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
       pc.mark(0);
 #pragma unroll
       for (int q = 0; q < SV; q++) {
-        const int j = t + q * kSampleNT;
+        const int j = t + q * NT;
         if (j < nvec) raw[q] = ldg_stream(vrow + j);
       }
       // the history hash (counts only) is built while the sample loads fly
       if (!risers) build_hist(0.0f, false);
 #pragma unroll
       for (int q = 0; q < SV; q++) {
-        const int j = t + q * kSampleNT;
+        const int j = t + q * NT;
         vm[q] = j < nvec ? vmax_of(raw[q], j) : neg_inf();
       }
       if (V > kCandMax && sampled > 0) {
         rk = rank_for(1.0f);
-        theta = sample_theta<SV>(vm, rk, sm);
+        theta = sample_theta<SV, NT>(vm, rk, sm);
       }
       if (t == 0) sm.cand_count = 0;
       __syncthreads();
       pc.mark(1);
 #pragma unroll
       for (int q = 0; q < SV; q++) {
-        const int j = t + q * kSampleNT;
+        const int j = t + q * NT;
         if (j < nvec && vm[q] >= theta) append_vec(raw[q], j, theta);
       }
       scalars(theta);
-      scan(theta, SV * kSampleNT);
+      scan(theta, SV * NT);
       fits = expand(theta);
     }
     pc.mark(2);
@@ -1136,7 +1149,7 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
         if (!hist.active) {
           build_hist(theta, risers);  // risers land after n0 with penalised values
         } else if (risers) {  // retry: append the risers for the new theta
-          for (int s = t; s < ht; s += kSampleNT) {
+          for (int s = t; s < ht; s += NT) {
             const int id = hkey[s];
             if (id < 0) continue;
             float raw = E::load(row, id);
@@ -1149,7 +1162,7 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
           }
           __syncthreads();
         }
-        for (int i = t; i < n0; i += kSampleNT) {  // raw -> penalised for history ids
+        for (int i = t; i < n0; i += NT) {  // raw -> penalised for history ids
           float hv;
           if (hist.find(cand_id[i], hv))
             cand_y[i] = hist_counts_only ? penalise(cand_y[i], __float_as_int(hv)) : hv;
@@ -1159,12 +1172,12 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
       pc.mark(3);
       const int cnt = sm.cand_count;
       const bool overflow = !fits || cnt > kCandMax;
-      SmemSrc src{cand_y, cand_id, cnt < kCandMax ? cnt : kCandMax, theta};
-      const unsigned int nvalid = block_count_if(src, theta, sm);
+      SmemSrcT<NT> src{cand_y, cand_id, cnt < kCandMax ? cnt : kCandMax, theta};
+      const unsigned int nvalid = block_count_if<NT>(src, theta, sm);
       if (t == 0) atomicAdd(&a.counters[5], static_cast<unsigned long long>(nvalid));
       pc.mark(4);
       if (a.shard_out && !overflow && nvalid >= need) {  // vocab shard: emit the local record
-        shard_emit(src, p, V, moff, a.shard_out + b, sm, theta > neg_inf() ? key2f(fkey(theta) - 1u) : neg_inf());
+        shard_emit<NT>(src, p, V, moff, a.shard_out + b, sm, theta > neg_inf() ? key2f(fkey(theta) - 1u) : neg_inf());
         return;
       }
       if (!overflow && nvalid >= need) {
@@ -1173,7 +1186,7 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
         if (partial) {  // exact mass of every finite element below theta (row re-read from L2)
           float ym = neg_inf();
           src.for_each([&](int, float y) { ym = fmaxf(ym, y); });
-          ym = block_max<kSampleNT>(ym, sm);
+          ym = block_max<NT>(ym, sm);
           const float T = p.temperature;
           const float smax = __fdiv_rn(ym, T);
           auto rest = [&](int v, float y) {
@@ -1191,16 +1204,16 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
             if (mask && !mask_allows(mask, moff + tail0 + t)) y = neg_inf();
             qrest += rest(tail0 + t, y);
           }
-          for (int j = t; j < nvec; j += kSampleNT) {
+          for (int j = t; j < nvec; j += NT) {
             float x[EPV];
             E::unpack(__ldg(vrow + j), x);
             const uint32_t bits = mask ? mask_bits(mask, moff + head + j * EPV, EPV) : 0xffu;
 #pragma unroll
             for (int e = 0; e < EPV; e++) qrest += rest(head + j * EPV + e, ((bits >> e) & 1u) ? x[e] : neg_inf());
           }
-          qrest = block_sum<kSampleNT>(qrest, sm);
+          qrest = block_sum<NT>(qrest, sm);
         }
-        done = finish_cands(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob, pc,
+        done = finish_cands<NT>(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob, pc,
                             partial, qrest);
         pc.mark(9);
         if (done) {
@@ -1217,7 +1230,7 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
       if (overflow) {  // the tgt-th largest of the buffered values bounds the k-th from below
         uint32_t tk; unsigned long long b0, m0; unsigned int c0, n0;
         const unsigned int tr = static_cast<unsigned int>(tgt);
-        radix_find<kSampleNT, true, false>(
+        radix_find<NT, true, false>(
             src, 32,
             [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; },
             [&](unsigned long long, unsigned int c) { return c >= tr; }, sm, tk, b0, c0, n0, m0, 16);
@@ -1228,10 +1241,10 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
         float vm[SV];
 #pragma unroll
         for (int q = 0; q < SV; q++) {
-          const int j = t + q * kSampleNT;
+          const int j = t + q * NT;
           vm[q] = j < nvec ? vmax_of(__ldg(vrow + j), j) : neg_inf();
         }
-        nt = sample_theta<SV>(vm, rk, sm);
+        nt = sample_theta<SV, NT>(vm, rk, sm);
         if (!(nt < theta)) nt = neg_inf();
       }
       theta = nt;
@@ -1248,12 +1261,12 @@ __global__ void __launch_bounds__(kSampleNT, kStream ? kStreamCtasPerSm : kMinCt
     if (t == 0) atomicAdd(&a.counters[4], 1ull);
     if (hist_counts_only) { hist.active = 0; __syncthreads(); }
     build_hist(__int_as_float(0x7f800000), true);
-    GlobalSrc<DT> src{row, V, head, nvec, tail0, mask, hist, moff};
+    GlobalSrc<DT, NT> src{row, V, head, nvec, tail0, mask, hist, moff};
     if (a.shard_out) {
-      shard_emit(src, p, V, moff, a.shard_out + b, sm, neg_inf());
+      shard_emit<NT>(src, p, V, moff, a.shard_out + b, sm, neg_inf());
       return;
     }
-    finish_row(src, p, V, u, false, neg_inf(), sm, out_id, out_prob);
+    finish_row<NT>(src, p, V, u, false, neg_inf(), sm, out_id, out_prob);
     pc.mark(11);
   }
   if (t == 0) {

@@ -131,7 +131,7 @@ __device__ __forceinline__ float smem_elem(const unsigned char* buf, int i) {
   return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(buf)[i]) << 16);
 }
 
-template <int DT>
+template <int DT, bool kMask>
 __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     spec_stats_kernel(SpecArgs a) {
   using E = Elt<DT>;
@@ -171,7 +171,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     row = reinterpret_cast<const char*>(a.draft) + (static_cast<int64_t>(b) * a.K + (pos - a.K - 1)) * V * E::kSize;
   }
   const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
-  const uint32_t* msk = spec_mask(a, b, pos <= a.K ? pos : pos - a.K - 1);
+  const uint32_t* msk = !kMask ? nullptr : spec_mask(a, b, pos <= a.K ? pos : pos - a.K - 1);
   // element i of the slice, -inf where the position's mask clears it
   auto elem = [&](int i) {
     const float x = smem_elem<DT>(slice, i);
@@ -238,7 +238,7 @@ __device__ __forceinline__ unsigned long long resid_mass(unsigned long long qT, 
 
 // One accept test of batch row b at position i (thread-level): appends to out
 // and sets fin to i on a stochastic reject, -2 on a greedy mismatch.
-template <int DT>
+template <int DT, bool kMask>
 __device__ __forceinline__ void spec_accept_step(const SpecArgs& a, int b, int i, int32_t* out,
                                                  int& n, int& fin) {
   using E = Elt<DT>;
@@ -255,7 +255,7 @@ __device__ __forceinline__ void spec_accept_step(const SpecArgs& a, int b, int i
     return;
   }
   bool accept = false;
-  const uint32_t* msk = spec_mask(a, b, i);
+  const uint32_t* msk = !kMask ? nullptr : spec_mask(a, b, i);
   if (tok >= 0 && tok < V && msk && !mask_allows(msk, tok)) {
     // a proposal the grammar does not allow is rejected
   } else if (tok >= 0 && tok < V) {
@@ -276,7 +276,7 @@ __device__ __forceinline__ void spec_accept_step(const SpecArgs& a, int b, int i
 }
 
 // Lazy mode: position i of every row still accepting, one thread per row.
-template <int DT>
+template <int DT, bool kMask>
 __global__ void __launch_bounds__(128) spec_chain_kernel(SpecArgs a, int i) {
   const int b = blockIdx.x * 128 + threadIdx.x;
   if (b >= a.batch) return;
@@ -289,12 +289,12 @@ __global__ void __launch_bounds__(128) spec_chain_kernel(SpecArgs a, int i) {
     fin = a.rstate[2 * b + 1];
     if (fin != -1) return;
   }
-  spec_accept_step<DT>(a, b, i, out, n, fin);
+  spec_accept_step<DT, kMask>(a, b, i, out, n, fin);
   a.rstate[2 * b] = n;
   a.rstate[2 * b + 1] = fin;
 }
 
-template <int DT>
+template <int DT, bool kMask>
 __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     spec_verify_kernel(SpecArgs a) {
   using E = Elt<DT>;
@@ -318,7 +318,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     int n = 0, fin = -1;
     if (!a.rstate) {
       for (int i = 0; i <= K; i++) out[i] = -1;
-      for (int i = 0; i < K && fin == -1; i++) spec_accept_step<DT>(a, b, i, out, n, fin);
+      for (int i = 0; i < K && fin == -1; i++) spec_accept_step<DT, kMask>(a, b, i, out, n, fin);
     } else if (K == 0) {
       out[0] = -1;
     } else {
@@ -353,7 +353,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
   const int sub = (c1 - c0 + kSpecNT - 1) / kSpecNT;
   const int v0 = min(c1, c0 + t * sub), v1 = min(c1, v0 + sub);
-  const uint32_t* msk = spec_mask(a, b, pos);
+  const uint32_t* msk = !kMask ? nullptr : spec_mask(a, b, pos);
   auto ld = [&](const char* row, int v) { return (msk && !mask_allows(msk, v)) ? neg_inf() : E::load(row, v); };
   auto qt_of = [&](int v) { return qmass(__fsub_rn(__fdiv_rn(ld(trow, v), T), smT)); };
   auto rq_of = [&](int v) {
@@ -408,8 +408,8 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
 // position i only for the rows still accepting, i = 0..K-1, each followed by
 // the accept test, then the bonus row of the rows that accepted everything,
 // then the draw (2K + 2 launches, fewer vocab rows read).
-template <int DT>
-inline cudaError_t launch_spec(SpecArgs a, cudaStream_t st) {
+template <int DT, bool kMask>
+inline cudaError_t launch_spec_t(SpecArgs a, cudaStream_t st) {
   const int esz = Elt<DT>::kSize;
   int chunk = (a.vocab + kSpecCluster - 1) / kSpecCluster;
   chunk = (chunk + 7) / 8 * 8;
@@ -417,24 +417,31 @@ inline cudaError_t launch_spec(SpecArgs a, cudaStream_t st) {
   const size_t stage = static_cast<size_t>(chunk) * esz;
   if (stage > static_cast<size_t>(kSpecMaxStage)) return cudaErrorInvalidValue;
   if (stage > 48 * 1024) {  // per device; cheap enough to repeat
-    cudaError_t e = cudaFuncSetAttribute(spec_stats_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(spec_stats_kernel<DT, kMask>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSpecMaxStage);
     if (e != cudaSuccess) return e;
   }
   if (!a.rstate) {
     const int nrows = a.batch * (2 * a.K + 1);
-    spec_stats_kernel<DT><<<nrows * kSpecCluster, kSpecNT, stage, st>>>(a);
+    spec_stats_kernel<DT, kMask><<<nrows * kSpecCluster, kSpecNT, stage, st>>>(a);
   } else {
     for (int i = 0; i < a.K; i++) {
       a.lazy_pos = i;
-      spec_stats_kernel<DT><<<a.batch * 2 * kSpecCluster, kSpecNT, stage, st>>>(a);
-      spec_chain_kernel<DT><<<(a.batch + 127) / 128, 128, 0, st>>>(a, i);
+      spec_stats_kernel<DT, kMask><<<a.batch * 2 * kSpecCluster, kSpecNT, stage, st>>>(a);
+      spec_chain_kernel<DT, kMask><<<(a.batch + 127) / 128, 128, 0, st>>>(a, i);
     }
     a.lazy_pos = a.K;
-    spec_stats_kernel<DT><<<a.batch * kSpecCluster, kSpecNT, stage, st>>>(a);
+    spec_stats_kernel<DT, kMask><<<a.batch * kSpecCluster, kSpecNT, stage, st>>>(a);
   }
-  spec_verify_kernel<DT><<<a.batch * kSpecCluster, kSpecNT, 0, st>>>(a);
+  spec_verify_kernel<DT, kMask><<<a.batch * kSpecCluster, kSpecNT, 0, st>>>(a);
   return cudaGetLastError();
+}
+
+// The masked kernels are separate instances, so the unmasked path carries no
+// mask code.
+template <int DT>
+inline cudaError_t launch_spec(SpecArgs a, cudaStream_t st) {
+  return a.state_ids ? launch_spec_t<DT, true>(a, st) : launch_spec_t<DT, false>(a, st);
 }
 
 }  // namespace tg

@@ -153,6 +153,10 @@ int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_s
     e = cudaFuncSetAttribute(tg::sample_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tg::sample_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tg::sample_kernel<0, false, tg::kWideNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tg::sample_kernel<1, false, tg::kWideNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   // the two-kernel mode serves rows longer than a candidate list, in batches of
   // kSplitMinBatch rows or more (TG_SAMPLE_SPLIT=0 turns it off)
   const char* split_env = getenv("TG_SAMPLE_SPLIT");
@@ -237,6 +241,22 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
   DeviceGuard g(s->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (s->profile) TG_CUDA(cudaEventRecord(s->prof_ev[0], st));
+  if (batch >= tg::kWideMinBatch && batch <= tg::kWideMaxBatch && s->vocab > tg::kCandMax) {
+    // few rows: one 1024-thread CTA per row, four times the warps on each row's
+    // latency-bound stages (the rest-of-row mass of rows without top-k above all);
+    // the warp rings follow the hash in shared memory
+    const size_t wsmem = smem + static_cast<size_t>(tg::kWideNT / 32) * tg::kRing * 20;
+    if (dtype == TG_DTYPE_F32)
+      tg::sample_kernel<0, false, tg::kWideNT><<<batch, tg::kWideNT, wsmem, st>>>(a);
+    else
+      tg::sample_kernel<1, false, tg::kWideNT><<<batch, tg::kWideNT, wsmem, st>>>(a);
+    TG_CUDA(cudaGetLastError());
+    if (s->profile) {
+      TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
+      s->prof_kind = 1;
+    }
+    return TG_OK;
+  }
   if (s->split_rows == 0 || batch < kSplitMinBatch) {
     if (dtype == TG_DTYPE_F32)
       tg::sample_kernel<0><<<batch, tg::kSampleNT, smem, st>>>(a);
