@@ -425,3 +425,24 @@ def test_tool_tags_fuzz_and_masks():
         n, o = g.state(), go.PaceToolTagFSM()
         assert n.accept_bytes(prefix) and o.accept_bytes(prefix)
         assert list(n.allowed()) == go.mask_ids(o, vocab), prefix
+
+
+def test_draft_state_rows():
+    """State rows for masked verification: row i is the state after drafts 0..i-1;
+    after a rejected draft the state stays; the live states are not advanced."""
+    from tinygpt_b200.grammar import draft_state_rows
+    vocab = [b'{"', b"name", b'":"', b"Al", b'"', b"x", b"}"]
+    g = Grammar(SIMPLE, vocab)
+    s0, s1 = g.state(), g.state()
+    drafts = np.array([[0, 1, 2, 3], [0, 6, 1, 2]], np.int32)  # row 1: '}' is rejected at i=1
+    rows = draft_state_rows([s0, s1], drafts)
+    ref = g.state()
+    expect0 = []
+    for t in [None, 0, 1, 2, 3]:
+        if t is not None:
+            assert ref.commit(t)
+        expect0.append(ref.row())
+    assert list(rows[0]) == expect0
+    assert rows[1, 0] == expect0[0] and rows[1, 1] == expect0[1]
+    assert list(rows[1, 2:]) == [rows[1, 1]] * 3
+    assert s0.row() == expect0[0] and s1.row() == expect0[0]
