@@ -59,9 +59,7 @@ def test_unaligned_row_stride(oracle_mod, sampler_factory, stride_pad):
         assert_same(oracle_mod, sampler_factory(V), w, stride=V + stride_pad, what="stride")
 
 
-def test_sorted_rows_force_full_row_path(oracle_mod, sampler_factory):
-    """Ascending / descending rows defeat the sampled threshold: the candidate
-    list overflows or comes up short and the full-row path must take over."""
+def _sorted_w():
     V = 128256
     B = 8
     base = np.linspace(-10, 10, V, dtype=np.float32)
@@ -70,13 +68,16 @@ def test_sorted_rows_force_full_row_path(oracle_mod, sampler_factory):
     p["temperature"] = [0.0, 0.0, 0.9, 0.9, 0.5, 0.5, 1.0, 1.0]
     p["top_k"] = [0, 0, 10, 10, 1000, 1000, 3, 3]
     p["top_p"] = [1.0, 1.0, 0.9, 0.9, 0.5, 0.5, 1.0, 1.0]
-    w = dict(logits=x, params=p, uniforms=W.rng(1).random(B, dtype=np.float32))
-    assert_same(oracle_mod, sampler_factory(V), w, what="sorted")
+    return dict(logits=x, params=p, uniforms=W.rng(1).random(B, dtype=np.float32))
 
 
-def test_ties_everywhere(oracle_mod, sampler_factory):
-    """Constant rows and two-level rows: top-k keeps all ties, top-p orders
-    ties by id, greedy returns the first maximum."""
+def test_sorted_rows_force_full_row_path(oracle_mod, sampler_factory):
+    """Ascending / descending rows defeat the sampled threshold: the candidate
+    list overflows or comes up short and the full-row path must take over."""
+    assert_same(oracle_mod, sampler_factory(128256), _sorted_w(), what="sorted")
+
+
+def _ties_w():
     V = 128256
     B = 12
     x = np.zeros((B, V), np.float32)
@@ -86,11 +87,16 @@ def test_ties_everywhere(oracle_mod, sampler_factory):
     p["temperature"] = [0.0, 1.0, 1.0, 1.0] * 3
     p["top_k"] = [0, 5, 0, 100] * 3
     p["top_p"] = [1.0, 0.3, 0.5, 0.9] * 3
-    w = dict(logits=x, params=p, uniforms=W.rng(2).random(B, dtype=np.float32))
-    assert_same(oracle_mod, sampler_factory(V), w, what="ties")
+    return dict(logits=x, params=p, uniforms=W.rng(2).random(B, dtype=np.float32))
 
 
-def test_penalties_edge_cases(oracle_mod, sampler_factory):
+def test_ties_everywhere(oracle_mod, sampler_factory):
+    """Constant rows and two-level rows: top-k keeps all ties, top-p orders
+    ties by id, greedy returns the first maximum."""
+    assert_same(oracle_mod, sampler_factory(128256), _ties_w(), what="ties")
+
+
+def _pen_w():
     V = 32000
     B = 32
     w, g = _base(B, V, 11, "bf16")
@@ -108,7 +114,51 @@ def test_penalties_edge_cases(oracle_mod, sampler_factory):
     w["history"] = hist
     w["history_len"] = g.integers(0, 301, size=B).astype(np.int32)
     w["history_len"][0] = 300
-    assert_same(oracle_mod, sampler_factory(V), w, what="penalties")
+    return w
+
+
+def test_penalties_edge_cases(oracle_mod, sampler_factory):
+    assert_same(oracle_mod, sampler_factory(32000), _pen_w(), what="penalties")
+
+
+def _tile(w, rows):
+    """The workload's rows repeated to `rows` rows (other uniforms per copy)."""
+    B = w["params"].shape[0]
+    reps = (rows + B - 1) // B
+    out = {}
+    for k, v in w.items():
+        if isinstance(v, np.ndarray) and k != "mask_table" and v.shape[:1] == (B,):
+            out[k] = np.concatenate([v] * reps)[:rows].copy()
+        else:
+            out[k] = v
+    out["uniforms"] = W.rng(rows).random(rows, dtype=np.float32)
+    return out
+
+
+@pytest.mark.parametrize("rows", [3, 160])
+@pytest.mark.parametrize("make", ["sorted", "ties", "penalties", "masks"])
+def test_edge_workloads_other_kernel_widths(oracle_mod, sampler_factory, make, rows):
+    """The edge workloads above run on the 1024-thread kernel (8-148 rows);
+    fewer and more rows take the 256-thread kernel."""
+    w = {"sorted": _sorted_w, "ties": _ties_w, "penalties": _pen_w, "masks": _masks_w}[make]()
+    V = w["logits"].shape[1]
+    assert_same(oracle_mod, sampler_factory(V), _tile(w, rows), what=f"{make} x{rows}")
+
+
+def _masks_w():
+    V = 128256
+    B = 16
+    w, g = _base(B, V, 5, "f32")
+    Wd = (V + 31) // 32
+    bits = np.zeros((4, Wd * 32), bool)
+    bits[1, :V] = g.random(V) < 0.001
+    bits[2, 12345] = True
+    bits[3, :V] = True
+    w["mask_table"] = W.pack_mask(bits)
+    w["state_id"] = np.array([0, 1, 2, 3, -1] * 3 + [1], np.int32)
+    w["params"]["temperature"] = np.where(np.arange(B) % 2 == 0, 0.0, 1.0)
+    w["params"]["top_k"] = np.where(np.arange(B) % 4 == 1, 50, 0)
+    return w
 
 
 def test_masks_and_bad_states(oracle_mod, sampler_factory):
