@@ -400,19 +400,26 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
                              const tg_row_params& p, int V, float u, BlockScratch& sm,
                              int& out_id, float& out_prob, PhaseClock& pc, bool partial = false,
                              unsigned long long q_rest = 0, float below_override = 0.0f,
-                             bool use_below = false) {
+                             bool use_below = false, bool have_range = false, float ymax_in = 0.0f,
+                             float nymin_in = 0.0f) {
   SmemSrcT<NT> src{cy, cid, n, theta};
   if (!(p.temperature > 0.0f)) return finish_row<NT>(src, p, V, u, false, theta, sm, out_id, out_prob);
   const float T = p.temperature;
   const bool topk = p.top_k > 0 && p.top_k < V;
   const int lane = threadIdx.x & 31;
 
-  float ymax = neg_inf(), nymin = neg_inf();
-  src.for_each([&](int, float y) {
-    ymax = fmaxf(ymax, y);
-    if (y > neg_inf()) nymin = fmaxf(nymin, -y);
-  });
-  block_max2<NT>(ymax, nymin, sm);
+  // largest value and minus the smallest finite one over the list (given by
+  // the caller when it already reduced them)
+  float ymax = ymax_in, nymin = nymin_in;
+  if (!have_range) {
+    ymax = neg_inf();
+    nymin = neg_inf();
+    src.for_each([&](int, float y) {
+      ymax = fmaxf(ymax, y);
+      if (y > neg_inf()) nymin = fmaxf(nymin, -y);
+    });
+    block_max2<NT>(ymax, nymin, sm);
+  }
   const float ymin = -nymin;
   if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return !partial; }
   // an upper bound of the values absent from the list
@@ -1085,6 +1092,9 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
     float theta = neg_inf();
     unsigned int rk = 0;
     bool fits;
+    bool fused = false;  // list penalised, counted and its range reduced on load
+    unsigned int f_cnt = 0;
+    float f_ymax = neg_inf(), f_nymin = neg_inf();
     if (pre) {
       pc.mark(0);
       if (!risers) build_hist(0.0f, false);
@@ -1094,11 +1104,43 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
       const int m = n < kCandMax ? n : kCandMax;
       const float* gy = a.cand_gy + static_cast<int64_t>(b) * kCandMax;
       const int* gid = a.cand_gid + static_cast<int64_t>(b) * kCandMax;
+      // the list arrives with the penalties applied, counted and with its range
+      // reduced in one pass (when penalties cannot raise a value)
+      fused = !(need_hist && risers);
+      unsigned long long cnt = 0;
+      float ymx = neg_inf(), nymn = neg_inf();
       for (int i = t; i < m; i += NT) {
-        cand_y[i] = __ldcs(gy + i);
-        cand_id[i] = __ldcs(gid + i);
+        float y = __ldcs(gy + i);
+        const int id = __ldcs(gid + i);
+        float hv;
+        if (fused && hist_counts_only && hist.find(id, hv)) y = penalise(y, __float_as_int(hv));
+        cand_y[i] = y;
+        cand_id[i] = id;
+        if (id >= 0 && y >= theta) {
+          cnt++;
+          ymx = fmaxf(ymx, y);
+          if (y > neg_inf()) nymn = fmaxf(nymn, -y);
+        }
       }
       if (t == 0) sm.cand_count = n;
+      if (fused) {  // one reduction of the three (its barriers also publish the list)
+        for (int o = 16; o > 0; o >>= 1) {
+          cnt += __shfl_xor_sync(kFull, cnt, o);
+          ymx = fmaxf(ymx, __shfl_xor_sync(kFull, ymx, o));
+          nymn = fmaxf(nymn, __shfl_xor_sync(kFull, nymn, o));
+        }
+        if ((t & 31) == 0) { sm.red_u64[t >> 5] = cnt; sm.red_f[t >> 5] = ymx; sm.red_f2[t >> 5] = nymn; }
+        __syncthreads();
+        f_cnt = 0;
+        f_ymax = neg_inf();
+        f_nymin = neg_inf();
+#pragma unroll
+        for (int i = 0; i < NT / 32; i++) {
+          f_cnt += static_cast<unsigned int>(sm.red_u64[i]);
+          f_ymax = fmaxf(f_ymax, sm.red_f[i]);
+          f_nymin = fmaxf(f_nymin, sm.red_f2[i]);
+        }
+      }
       __syncthreads();
       fits = true;
       pc.mark(1);
@@ -1144,7 +1186,7 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
     }
 
     for (int attempt = 0;; attempt++) {
-      if (need_hist) {
+      if (need_hist && !fused) {
         const int n0 = sm.cand_count < kCandMax ? sm.cand_count : kCandMax;  // raw entries
         if (!hist.active) {
           build_hist(theta, risers);  // risers land after n0 with penalised values
@@ -1173,7 +1215,7 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
       const int cnt = sm.cand_count;
       const bool overflow = !fits || cnt > kCandMax;
       SmemSrcT<NT> src{cand_y, cand_id, cnt < kCandMax ? cnt : kCandMax, theta};
-      const unsigned int nvalid = block_count_if<NT>(src, theta, sm);
+      const unsigned int nvalid = fused ? f_cnt : block_count_if<NT>(src, theta, sm);
       if (t == 0) atomicAdd(&a.counters[5], static_cast<unsigned long long>(nvalid));
       pc.mark(4);
       if (a.shard_out && !overflow && nvalid >= need) {  // vocab shard: emit the local record
@@ -1214,7 +1256,7 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
           qrest = block_sum<NT>(qrest, sm);
         }
         done = finish_cands<NT>(cand_y, cand_id, cand_e, src.n, theta, p, V, u, sm, out_id, out_prob, pc,
-                            partial, qrest);
+                                partial, qrest, 0.0f, false, fused, f_ymax, f_nymin);
         pc.mark(9);
         if (done) {
           if (t == 0) atomicAdd(&a.counters[0], 1ull);
@@ -1224,6 +1266,7 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
       } else if (t == 0) {
         atomicAdd(&a.counters[overflow ? 1 : 2], 1ull);
       }
+      fused = false;  // a retry rebuilds the list from raw values
       if (attempt == kRetries || theta == neg_inf()) break;
       // retry from L2 with a new threshold
       float nt;
