@@ -1097,7 +1097,6 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
     float f_ymax = neg_inf(), f_nymin = neg_inf();
     if (pre) {
       pc.mark(0);
-      if (!risers) build_hist(0.0f, false);
       if (V > kCandMax && sampled > 0) rk = rank_for(1.0f);
       theta = a.cand_gth[b];
       const int n = a.cand_gn[b];
@@ -1105,21 +1104,40 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
       const float* gy = a.cand_gy + static_cast<int64_t>(b) * kCandMax;
       const int* gid = a.cand_gid + static_cast<int64_t>(b) * kCandMax;
       // the list arrives with the penalties applied, counted and with its range
-      // reduced in one pass (when penalties cannot raise a value)
+      // reduced in one pass (when penalties cannot raise a value); the first
+      // batch of loads is issued before the history hash is built
       fused = !(need_hist && risers);
+      constexpr int LU = 4;
+      float yv[LU];
+      int iv[LU];
+      auto load_batch = [&](int base) {
+#pragma unroll
+        for (int q = 0; q < LU; q++) {
+          const int i = base + q * NT + t;
+          if (i < m) { yv[q] = __ldcs(gy + i); iv[q] = __ldcs(gid + i); }
+        }
+      };
+      load_batch(0);
+      if (!risers) build_hist(0.0f, false);
       unsigned long long cnt = 0;
       float ymx = neg_inf(), nymn = neg_inf();
-      for (int i = t; i < m; i += NT) {
-        float y = __ldcs(gy + i);
-        const int id = __ldcs(gid + i);
-        float hv;
-        if (fused && hist_counts_only && hist.find(id, hv)) y = penalise(y, __float_as_int(hv));
-        cand_y[i] = y;
-        cand_id[i] = id;
-        if (id >= 0 && y >= theta) {
-          cnt++;
-          ymx = fmaxf(ymx, y);
-          if (y > neg_inf()) nymn = fmaxf(nymn, -y);
+      for (int base = 0; base < m; base += LU * NT) {
+        if (base > 0) load_batch(base);
+#pragma unroll
+        for (int q = 0; q < LU; q++) {
+          const int i = base + q * NT + t;
+          if (i >= m) break;
+          float y = yv[q];
+          const int id = iv[q];
+          float hv;
+          if (fused && hist_counts_only && hist.find(id, hv)) y = penalise(y, __float_as_int(hv));
+          cand_y[i] = y;
+          cand_id[i] = id;
+          if (id >= 0 && y >= theta) {
+            cnt++;
+            ymx = fmaxf(ymx, y);
+            if (y > neg_inf()) nymn = fmaxf(nymn, -y);
+          }
         }
       }
       if (t == 0) sm.cand_count = n;
