@@ -222,3 +222,44 @@ def test_no_topk_truncation_modes(oracle_mod, sampler_factory, scale):
     p["presence_penalty"] = 0.4
     p["frequency_penalty"] = 0.2
     assert_same(oracle_mod, sampler_factory(V), w, what=f"no-topk scale={scale}")
+
+
+def _nok_w(V, B, seed, dtype):
+    """Rows without top-k that reach the full-row stages: no truncation at all,
+    top-p cuts beyond any candidate list (flat rows, p close to 1), p = 0,
+    min-p, ties, penalties raising and lowering values, masked rows."""
+    w, g = _base(B, V, seed, dtype, scale=1.0)
+    x = W.bf16_bits_to_f32(w["logits"]) if dtype == "bf16" else w["logits"]
+    x = x.copy()
+    x[0] = 0.0                                  # one constant row
+    x[1, ::7] = 2.0                             # two levels
+    x[2] *= 0.05                                # nearly flat
+    if B > 3:
+        x[3] = np.linspace(-8, 8, V, dtype=np.float32)  # sorted
+    w["logits"] = W.to_bf16_bits(x) if dtype == "bf16" else x
+    p = w["params"]
+    p["top_k"] = 0
+    p["temperature"] = g.choice([0.5, 1.0, 2.0], size=B)
+    p["top_p"] = g.choice([1.0, 0.9999, 0.99, 0.95, 0.5, 0.0], size=B)
+    p["min_p"] = g.choice([0.0, 0.0, 0.05], size=B)
+    p["repetition_penalty"] = g.choice([1.0, 1.3], size=B)
+    p["presence_penalty"] = g.choice([0.0, 0.5, -0.7], size=B)
+    hist = g.integers(0, V, size=(B, 64)).astype(np.int32)
+    w["history"] = hist
+    w["history_len"] = g.integers(0, 65, size=B).astype(np.int32)
+    Wd = (V + 31) // 32
+    bits = g.random((3, Wd * 32)) < np.array([[0.5], [0.02], [1.0]])
+    bits[:, V:] = False
+    w["mask_table"] = W.pack_mask(bits)
+    w["state_id"] = g.integers(-1, 3, size=B).astype(np.int32)
+    return w
+
+
+@pytest.mark.parametrize("V,dtype,B", [(128256, "bf16", 16), (128256, "f32", 3), (50021, "f32", 160),
+                                        (50021, "bf16", 16)])
+def test_full_row_stages_without_topk(oracle_mod, sampler_factory, V, dtype, B):
+    w = _nok_w(V, B, V + B, dtype)
+    s = sampler_factory(V)
+    s.path_counters()
+    assert_same(oracle_mod, s, w, what=f"no-top-k full rows V={V} {dtype} B={B}")
+    assert s.path_counters()["full_row"] > 0

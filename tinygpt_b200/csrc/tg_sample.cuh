@@ -156,6 +156,24 @@ struct GlobalSrc {
   const uint32_t* mask;
   Hist hist;
   int moff;  // bit offset of element 0 in the mask row (vocab shards)
+  // value of element v (raw x): penalised, or -inf where masked
+  __device__ __forceinline__ float value(int v, float x) const {
+    float y;
+    if (!hist.find(v, y)) y = (mask && !mask_allows(mask, v + moff)) ? neg_inf() : x;
+    return y;
+  }
+  // values of vector j (elements head + j*EPV ...)
+  __device__ __forceinline__ void vec(int j, float* y) const {
+    using E = Elt<DT>;
+    constexpr int EPV = E::kEPV;
+    float x[EPV];
+    E::unpack(__ldg(reinterpret_cast<const uint4*>(row + head * E::kSize) + j), x);
+    const int e0 = head + j * EPV;
+    const uint32_t bits = mask ? mask_bits(mask, e0 + moff, EPV) : 0xffu;
+#pragma unroll
+    for (int e = 0; e < EPV; e++)
+      if (!hist.find(e0 + e, y[e])) y[e] = ((bits >> e) & 1u) ? x[e] : neg_inf();
+  }
   template <class F>
   __device__ __forceinline__ void for_each(F&& f) const {
     using E = Elt<DT>;
@@ -258,6 +276,15 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
   ymax = block_max<NT>(ymax, sm);
   if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
   const float smax = __fdiv_rn(ymax, T);
+  // y <= ylim implies y/T - smax <= -31.9, a zero mass (tg_exp(-31) * 2^44 < 1):
+  // the rounding of ylim, y/T and the difference stays below 0.1 while
+  // |smax| < 1e5.  Zero-mass elements change no sum, cut or draw, so their
+  // division and exponential are skipped.
+  const float ylim = __fmul_rn(__fsub_rn(smax, 32.0f), T);
+  const bool use_lim = fabsf(smax) < 1.0e5f;
+  auto mass = [&](float y, float s) {
+    return (use_lim && !(y > ylim)) ? 0ull : qmass(__fsub_rn(s, smax));
+  };
 
   auto inA = [&](float y, float& s) {
     if (!(y > neg_inf())) return false;
@@ -267,8 +294,9 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
 
   unsigned long long Q = 0;
   src.for_each([&](int, float y) {
+    if (!topk && use_lim && !(y > ylim)) return;  // zero mass
     float s;
-    if (inA(y, s)) Q += qmass(__fsub_rn(s, smax));
+    if (inA(y, s)) Q += mass(y, s);
   });
   Q = block_sum<NT>(Q, sm);
 
@@ -298,7 +326,7 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
             float s;
             if (!inA(y, s)) return false;
             key = fkey(s);
-            w = qmass(__fsub_rn(s, smax));
+            w = mass(y, s);
             return true;
           },
           [&](unsigned long long m, unsigned int) { return __ull2double_rn(m) >= tau; }, sm,
@@ -341,7 +369,7 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
       const uint32_t k = fkey(s);
       if (k < cut_key || (k == cut_key && id > cut_id)) return false;
     }
-    q = qmass(__fsub_rn(s, smax));
+    q = mass(y, s);
     return !minpon || __ull2double_rn(q) >= minq;
   };
 
@@ -363,6 +391,256 @@ __device__ bool finish_row(const Src& src, const tg_row_params& p, int V, float 
       },
       [&](unsigned long long m, unsigned int) { return m > r; }, sm, pick, b2, c2, n2, qpick);
   out_id = static_cast<int>(pick);
+  out_prob = __double2float_rn(__ddiv_rn(__ull2double_rn(qpick), __ull2double_rn(S)));
+  return true;
+}
+
+// Full-row stages for a stochastic row without top-k (top-p, min-p or neither),
+// in four passes over the row:
+//   1. the maximum;
+//   2. (top-p) the masses into a 1024-bin histogram over smax - s (32 bins per
+//      unit, 32-bit limb atomics) and their total Q; the bin where the mass in
+//      (s desc) order reaches top_p * Q is collected into shared memory and the
+//      cut (key, id) resolved there exactly;
+//   3. the final masses (top-p cut, min-p), summed per 128-bit-vector iteration
+//      into a shared table (index order is iteration-major), and their total S;
+//   4. the draw point's iteration recomputed: a block scan over its vectors and
+//      one thread's scan of its own vector give the id.
+// Same arithmetic as finish_row; returns false (nothing written) when the
+// crossing bin holds more than `cap` elements or the table does not fit.
+template <int DT, int NT>
+__device__ bool finish_full(const GlobalSrc<DT, NT>& g, const tg_row_params& p, float u, BlockScratch& sm,
+                            unsigned char* scratch, int cap, int& out_id, float& out_prob) {
+  using E = Elt<DT>;
+  constexpr int EPV = E::kEPV;
+  const int t = threadIdx.x;
+  const int niter = (g.nvec + NT - 1) / NT;
+  if (niter > 4 * NT) return false;  // the table scan covers 4 iterations per thread
+  float ymax = neg_inf();
+  g.for_each([&](int, float y) { ymax = fmaxf(ymax, y); });
+  ymax = block_max<NT>(ymax, sm);
+  if (ymax == neg_inf()) { out_id = -1; out_prob = 0.0f; return true; }
+  const float T = p.temperature;
+  const float smax = __fdiv_rn(ymax, T);
+  const float ylim = __fmul_rn(__fsub_rn(smax, 32.0f), T);  // zero mass at or below (see finish_row)
+  const bool use_lim = fabsf(smax) < 1.0e5f;
+  // mass and tempered value of value y (0 for -inf and provably zero masses)
+  auto qs = [&](float y, float& sv) -> unsigned long long {
+    if (!(y > neg_inf()) || (use_lim && !(y > ylim))) return 0ull;
+    sv = __fdiv_rn(y, T);
+    return qmass(__fsub_rn(sv, smax));
+  };
+  auto dbin = [&](float sv) {
+    const int bn = static_cast<int>(__fmul_rn(__fsub_rn(smax, sv), 32.0f));
+    return bn > 1023 ? 1023 : bn;
+  };
+  float* my = reinterpret_cast<float*>(scratch);
+  int* mid = reinterpret_cast<int*>(scratch + static_cast<size_t>(cap) * 4);
+
+  const bool toppon = p.top_p < 1.0f;
+  uint32_t cut_key = 0;
+  int cut_id = 0x7fffffff;
+  if (toppon) {
+    hist_zero<NT, 1024, true>(sm);
+    __syncthreads();
+    unsigned long long Q = 0;
+    g.for_each([&](int, float y) {
+      float sv;
+      const unsigned long long q = qs(y, sv);
+      if (q) { Q += q; hist_put<true>(sm, dbin(sv), q); }
+    });
+    Q = block_sum<NT>(Q, sm);
+    const double tau = __dmul_rn(static_cast<double>(p.top_p), __ull2double_rn(Q));
+    if (!(tau > 0.0)) {  // the single top element: the smallest id holding the maximum
+      cut_key = fkey(smax);
+      unsigned int best = 0u;
+      g.for_each([&](int v, float y) {
+        if (y == ymax) best = max(best, ~static_cast<uint32_t>(v));
+      });
+      cut_id = static_cast<int>(~block_max_u32<NT>(best, sm));
+    } else {
+      const HistSel hs = hist_scan<NT, 1024, true>([&](unsigned long long m) { return __ull2double_rn(m) >= tau; }, sm);
+      if (t == 0) sm.cand_count = 0;
+      __syncthreads();
+      g.for_each([&](int v, float y) {
+        float sv;
+        if (qs(y, sv) == 0 || dbin(sv) != hs.bin) return;
+        const int pos = atomicAdd(&sm.cand_count, 1);
+        if (pos < cap) { my[pos] = sv; mid[pos] = v; }
+      });
+      __syncthreads();
+      const int m = sm.cand_count;
+      __syncthreads();
+      if (m > cap) return false;
+      SmemSrcT<NT> ms{my, mid, m, neg_inf()};
+      unsigned long long above = 0, qt = 0;
+      unsigned int nties = 0, cb;
+      unsigned long long jstar = 1;
+      const unsigned long long before = hs.before;
+      radix_find<NT, true, true>(
+          ms, 32,
+          [&](int, float sv, uint32_t& key, unsigned long long& w) {
+            key = fkey(sv);
+            w = qmass(__fsub_rn(sv, smax));
+            return true;
+          },
+          [&](unsigned long long mm, unsigned int) { return __ull2double_rn(before + mm) >= tau; }, sm,
+          cut_key, above, cb, nties, qt);
+      above += before;
+      qt = qmass(__fsub_rn(key2f(cut_key), smax));
+      if (qt > 0) {
+        const double need = tau - __ull2double_rn(above);
+        if (need > 0.0) {
+          const double est = ceil(__ddiv_rn(need, __ull2double_rn(qt)));
+          jstar = est < 1.0 ? 1ull : static_cast<unsigned long long>(est);
+        }
+        if (jstar > nties) jstar = nties;
+        while (jstar > 1 && __ull2double_rn(above + (jstar - 1) * qt) >= tau) jstar--;
+        while (jstar < nties && __ull2double_rn(above + jstar * qt) < tau) jstar++;
+      }
+      if (jstar < nties) {
+        uint32_t idkey; unsigned long long b1, m1; unsigned int c1, n1;
+        const unsigned int js = static_cast<unsigned int>(jstar);
+        radix_find<NT, false, false>(
+            ms, 20,
+            [&](int id, float sv, uint32_t& key, unsigned long long& w) {
+              if (fkey(sv) != cut_key) return false;
+              key = static_cast<uint32_t>(id);
+              w = 0;
+              return true;
+            },
+            [&](unsigned long long, unsigned int c) { return c >= js; }, sm, idkey, b1, c1, n1, m1);
+        cut_id = static_cast<int>(idkey);
+      }
+    }
+  }
+  const bool minpon = p.min_p > 0.0f;
+  const double minq = __dmul_rn(static_cast<double>(fminf(p.min_p, 1.0f)), static_cast<double>(kMassScale));
+  auto fin = [&](int v, float y) -> unsigned long long {  // final mass of element v
+    float sv;
+    const unsigned long long q = qs(y, sv);
+    if (q == 0) return 0ull;
+    if (toppon) {
+      const uint32_t k = fkey(sv);
+      if (k < cut_key || (k == cut_key && v > cut_id)) return 0ull;
+    }
+    return (!minpon || __ull2double_rn(q) >= minq) ? q : 0ull;
+  };
+  // pass 3: per-iteration sums (three 15/15/22-bit limbs of each warp's sum)
+  unsigned int* tab = reinterpret_cast<unsigned int*>(scratch);
+  __syncthreads();  // the member list is no longer needed
+  for (int i = t; i < 3 * niter; i += NT) tab[i] = 0u;
+  __syncthreads();
+  unsigned long long sh = 0, sv8 = 0, stl = 0;
+  if (t < g.head) sh = fin(t, g.value(t, E::load(g.row, t)));
+  if (t < g.V - g.tail0) stl = fin(g.tail0 + t, g.value(g.tail0 + t, E::load(g.row, g.tail0 + t)));
+  for (int it = 0; it < niter; it++) {
+    const int j = it * NT + t;
+    unsigned long long w = 0;
+    if (j < g.nvec) {
+      float y[EPV];
+      g.vec(j, y);
+#pragma unroll
+      for (int e = 0; e < EPV; e++) w += fin(g.head + j * EPV + e, y[e]);
+    }
+    sv8 += w;
+    for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(kFull, w, o);
+    if ((t & 31) == 0 && w) {
+      atomicAdd(&tab[it], static_cast<unsigned>(w & 0x7fffu));
+      atomicAdd(&tab[niter + it], static_cast<unsigned>((w >> 15) & 0x7fffu));
+      atomicAdd(&tab[2 * niter + it], static_cast<unsigned>(w >> 30));
+    }
+  }
+  const unsigned long long H = block_sum<NT>(sh, sm);
+  const unsigned long long S = block_sum<NT>(sh + sv8 + stl, sm);
+  const unsigned long long r = draw_point(u, S);
+  auto tab_at = [&](int it) {
+    return static_cast<unsigned long long>(tab[it]) + (static_cast<unsigned long long>(tab[niter + it]) << 15) +
+           (static_cast<unsigned long long>(tab[2 * niter + it]) << 30);
+  };
+  int pick = -1;
+  unsigned long long qpick = 0;
+  if (r < H) {  // in the scalar head: thread 0 scans it
+    if (t == 0) {
+      unsigned long long c = 0;
+      for (int v = 0; v < g.head; v++) {
+        const unsigned long long q = fin(v, g.value(v, E::load(g.row, v)));
+        c += q;
+        if (c > r) { pick = v; qpick = q; break; }
+      }
+      sm.sid[0] = pick; sm.sel_before = qpick;
+    }
+    __syncthreads();
+    pick = sm.sid[0]; qpick = sm.sel_before;
+    __syncthreads();
+  } else {
+    // the iteration holding r - H: a block scan over the table
+    const unsigned long long r1 = r - H;
+    constexpr int kPer = 4;
+    unsigned long long loc = 0, vals[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; k++) {
+      const int it = t * kPer + k;
+      vals[k] = it < niter ? tab_at(it) : 0ull;
+      loc += vals[k];
+    }
+    unsigned long long tot;
+    const unsigned long long bef = block_excl_scan<NT>(loc, tot, sm);
+    if (t == 0) { sm.sel_bin = 0xffffffffu; }
+    __syncthreads();
+    if (r1 >= bef && r1 < bef + loc) {
+      unsigned long long c = bef;
+#pragma unroll
+      for (int k = 0; k < kPer; k++) {
+        if (r1 < c + vals[k]) { sm.sel_bin = t * kPer + k; sm.sel_before = c; break; }
+        c += vals[k];
+      }
+    }
+    __syncthreads();
+    const unsigned int its = sm.sel_bin;
+    const unsigned long long ibefore = sm.sel_before;
+    __syncthreads();
+    if (its != 0xffffffffu) {
+      const unsigned long long r2 = r1 - ibefore;
+      const int j = static_cast<int>(its) * NT + t;
+      float y[EPV];
+      unsigned long long q8[EPV], w = 0;
+      if (j < g.nvec) {
+        g.vec(j, y);
+#pragma unroll
+        for (int e = 0; e < EPV; e++) { q8[e] = fin(g.head + j * EPV + e, y[e]); w += q8[e]; }
+      }
+      unsigned long long tw;
+      const unsigned long long wb = block_excl_scan<NT>(w, tw, sm);
+      if (w > 0 && r2 >= wb && r2 < wb + w) {
+        unsigned long long c = wb;
+#pragma unroll
+        for (int e = 0; e < EPV; e++) {
+          c += q8[e];
+          if (c > r2) { sm.sid[0] = g.head + j * EPV + e; sm.sel_mass = q8[e]; break; }
+        }
+      }
+      __syncthreads();
+      pick = sm.sid[0];
+      qpick = sm.sel_mass;
+      __syncthreads();
+    } else {  // past the vectors: the scalar tail, scanned by thread 0
+      const unsigned long long r2 = r1 - tot;
+      if (t == 0) {
+        unsigned long long c = 0;
+        for (int v = g.tail0; v < g.V; v++) {
+          const unsigned long long q = fin(v, g.value(v, E::load(g.row, v)));
+          c += q;
+          if (c > r2) { pick = v; qpick = q; break; }
+        }
+        sm.sid[0] = pick; sm.sel_before = qpick;
+      }
+      __syncthreads();
+      pick = sm.sid[0]; qpick = sm.sel_before;
+      __syncthreads();
+    }
+  }
+  out_id = pick;
   out_prob = __double2float_rn(__ddiv_rn(__ull2double_rn(qpick), __ull2double_rn(S)));
   return true;
 }
@@ -1249,7 +1527,12 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
           ym = block_max<NT>(ym, sm);
           const float T = p.temperature;
           const float smax = __fdiv_rn(ym, T);
+          // y <= ylim: zero mass (as in finish_row); the raw value bounds the
+          // penalised one unless penalties can raise it
+          const float ylim = __fmul_rn(__fsub_rn(smax, 32.0f), T);
+          const bool use_lim = !(hist.active && !hist_counts_only) && fabsf(smax) < 1.0e5f;
           auto rest = [&](int v, float y) {
+            if (use_lim && !(y > ylim)) return 0ull;
             float hv;
             if (hist.active && hist.find(v, hv)) y = hist_counts_only ? penalise(y, __float_as_int(hv)) : hv;
             return (y < theta && y > neg_inf()) ? qmass(__fsub_rn(__fdiv_rn(y, T), smax)) : 0ull;
@@ -1327,7 +1610,9 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
       shard_emit<NT>(src, p, V, moff, a.shard_out + b, sm, neg_inf());
       return;
     }
-    finish_row<NT>(src, p, V, u, false, neg_inf(), sm, out_id, out_prob);
+    const bool nok_stochastic = p.temperature > 0.0f && !(p.top_k > 0 && p.top_k < V);
+    if (!(nok_stochastic && finish_full<DT, NT>(src, p, u, sm, dyn, kCandMax, out_id, out_prob)))
+      finish_row<NT>(src, p, V, u, false, neg_inf(), sm, out_id, out_prob);
     pc.mark(11);
   }
   if (t == 0) {
