@@ -203,6 +203,11 @@ def run_config(args):
     Vc, Bc = c["vocab"], c["batch"]
     s = Sampler(Vc, Bc, 0)
     sets = [W.make(cfg, seed=1 + i) for i in range(2 if cfg in (3, 4) else 1)]
+    if args.variant != "none":  # the same rows without top-k (top-p only, or plain temperature)
+        for w in sets:
+            w["params"]["top_k"] = 0
+            if args.variant == "temp":
+                w["params"]["top_p"] = 1.0
 
     def to_dev(w):
         d = {}
@@ -264,7 +269,9 @@ def run_config(args):
     peak, peak_kind = measured_peak()
     bytes_call = W.bytes_per_row(cfg) * Bc
     achieved = bytes_call / (us * 1e-6) / 1e9
-    line = {"metric": f"config {cfg} ({c['name']}): device time per call", "value": us, "unit": "us",
+    name = c["name"] + ("" if args.variant == "none" else f", {args.variant} variant (top_k = 0"
+                        + (", top_p = 1" if args.variant == "temp" else "") + ")")
+    line = {"metric": f"config {cfg} ({name}): device time per call", "value": us, "unit": "us",
             "higher_is_better": False, "n_gpus": 1, "steps": calls, "warmup": args.warmup,
             "rows_per_s": Bc / (us * 1e-6), "dtype": c["dtype"],
             "data": "synthetic (tinygpt_b200.workloads, seeded Philox)",
@@ -291,6 +298,8 @@ def main():
                     help="untimed steps whose per-kernel CUDA-event times give the roofline")
     ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
                     help="1-5: one line for that workload's call time (one GPU) instead of the headline")
+    ap.add_argument("--variant", default="none", choices=["none", "topp", "temp"],
+                    help="with --config 1-4: the same rows without top-k (topp) or with temperature only (temp)")
     args = ap.parse_args()
     if args.config:
         run_config(args)
