@@ -110,7 +110,11 @@ int32_t tg_sampler_destroy(tg_sampler* s);
  *   out_ids      [batch] int32; -1 where no token is admissible
  *   out_probs    [batch] float probability of the chosen id under the final
  *                distribution (1 for greedy rows), may be NULL
- * Asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream).
+ * Asynchronous on `stream` (a cudaStream_t, NULL = legacy default stream);
+ * allocates nothing.  The launch shape depends on the batch and never changes
+ * a result: 8..148 rows run one 1024-thread CTA per row; 1024 rows or more run
+ * two kernels (the stream to the handle's candidate buffer, then selection);
+ * other batches run one 256-thread CTA per row.
  * Replaces: python_ref/model.py:213-224, wasm/src/model.cpp:489-517,
  *           Serve.swift:1483-1506, ModelController.swift:262-304. */
 int32_t tg_sample(tg_sampler* s, const void* logits, int32_t dtype,

@@ -29,13 +29,10 @@
 
 namespace tg {
 
-#ifndef TG_NT
-#define TG_NT 256
-#endif
 #ifndef TG_CAND_MAX
 #define TG_CAND_MAX 2816
 #endif
-constexpr int kSampleNT = TG_NT;        // threads per CTA
+constexpr int kSampleNT = 256;         // threads per CTA (the default; kernels take NT)
 constexpr int kCandMax = TG_CAND_MAX;   // candidate list capacity
 constexpr int kFastMaxK = 1024;  // largest top-k served by the candidate path
 constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold sample
