@@ -244,6 +244,24 @@ int32_t tg_sample_shard_merge(tg_sampler* s, const tg_shard_record* records, int
                               const float* uniforms, int32_t* out_ids, float* out_probs,
                               void* stream);
 
+/* Vocab-sharded sampling in one call: the local half (this handle's vocab is the
+ * slice [vocab_offset, vocab_offset + vocab) of rows of full_vocab ids), one
+ * ncclAllGather of the per-row records over `nccl_comm` (an ncclComm_t of
+ * nranks ranks, this rank's slice in rank order), and the merge, all on
+ * `stream`; every rank gets the same ids.  Arguments otherwise as tg_sample,
+ * for this rank's slice of every row.  NCCL is not linked: ncclAllGather is
+ * looked up in the NCCL the process has loaded (TG_ERR_UNSUPPORTED if none).
+ * Record storage ((nranks + 1) x batch x 10,256 bytes) is allocated on the
+ * first call and grows with batch and nranks.  Limits as the two halves
+ * (tg_sample_shard_local / tg_sample_shard_merge).  No counterpart in the
+ * reference, which samples every row on one device. */
+int32_t tg_sample_sharded(tg_sampler* s, void* nccl_comm, int32_t nranks, int32_t vocab_offset,
+                          int32_t full_vocab, const void* logits, int32_t dtype, int64_t row_stride,
+                          int32_t batch, const tg_row_params* params, const int32_t* history,
+                          const int32_t* history_len, int32_t history_stride,
+                          const uint32_t* mask_table, int32_t num_states, const int32_t* state_id,
+                          const float* uniforms, int32_t* out_ids, float* out_probs, void* stream);
+
 /* Device error word of the last completed call on this handle (synchronizes
  * the handle's device).  Bit 0: a state_id outside [0, num_states);
  * bit 1: a draft id outside [0, vocab); bit 2: a row the vocab-sharded mode

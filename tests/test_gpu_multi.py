@@ -1,6 +1,6 @@
 """Two GPUs, one process each, NCCL over NVLink: the vocab-sharded path with a
-real all-gather (tinygpt_b200.dist.sample_vocab_sharded) equals the oracle on
-whole rows; skipped when fewer than two GPUs are visible."""
+real all-gather (tinygpt_b200.dist.sample_vocab_sharded, and the one-call
+tg_sample_sharded on an NCCL communicator) equals the oracle on whole rows; skipped when fewer than two GPUs are visible."""
 import os
 
 import numpy as np
@@ -32,7 +32,17 @@ def _worker(rank, world, port, out_path):
             history=torch.from_numpy(w["history"]).to(dev),
             history_len=torch.from_numpy(w["history_len"]).to(dev))
         torch.cuda.synchronize()
+        # the same through the one-call C entry point and our own NCCL communicator
+        from tinygpt_b200.dist import NcclComm
+        comm = NcclComm(rank, world, rank)
+        ids2, _ = s.sample_sharded(
+            comm.ptr, world, L, w["params"], lo, V, uniforms=torch.from_numpy(w["uniforms"]).to(dev),
+            history=torch.from_numpy(w["history"]).to(dev),
+            history_len=torch.from_numpy(w["history_len"]).to(dev))
+        torch.cuda.synchronize()
+        comm.close()
     np.save(out_path + f".{rank}.npy", ids.cpu().numpy())
+    np.save(out_path + f".c{rank}.npy", ids2.cpu().numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -48,3 +58,4 @@ def test_vocab_sharded_two_gpus_nccl(oracle_mod, tmp_path):
     want, _ = oracle_sample(oracle_mod, W.make(4, seed=9, batch=64))
     for r in range(2):
         assert np.array_equal(np.load(out + f".{r}.npy"), want)
+        assert np.array_equal(np.load(out + f".c{r}.npy"), want)

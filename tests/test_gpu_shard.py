@@ -56,3 +56,25 @@ def test_sharded_greedy_masks_and_unsupported_rows(oracle_mod, sampler_factory):
     assert np.array_equal(gi[ok], oi[ok])
     assert np.array_equal(gp[ok].view(np.uint32), op[ok].view(np.uint32))
     assert gi[5] == -1 and m.device_status() & 4
+
+
+def test_sample_sharded_one_rank_communicator(oracle_mod, sampler_factory):
+    """tg_sample_sharded on a one-rank NCCL communicator (local records, all-gather,
+    merge in one call) equals the oracle on whole rows."""
+    import torch
+    from tinygpt_b200.dist import NcclComm
+    from tests.gpu_helpers import logits_to_dev, oracle_sample
+    w = W.make(4, seed=13, batch=48)
+    V = w["vocab"]
+    s = sampler_factory(V)
+    comm = NcclComm(0, 1, 0)
+    try:
+        ids, _ = s.sample_sharded(comm.ptr, 1, logits_to_dev(w["logits"]), w["params"], 0, V,
+                                  uniforms=torch.from_numpy(w["uniforms"]).cuda(),
+                                  history=torch.from_numpy(w["history"]).cuda(),
+                                  history_len=torch.from_numpy(w["history_len"]).cuda())
+        torch.cuda.synchronize()
+    finally:
+        comm.close()
+    want, _ = oracle_sample(oracle_mod, w)
+    assert np.array_equal(ids.cpu().numpy(), want)

@@ -37,7 +37,7 @@ ROW_PARAMS_DTYPE = np.dtype([
 
 EXPORTED = ["tg_abi_version", "tg_last_error_string", "tg_sampler_create", "tg_sampler_destroy",
             "tg_sample", "tg_sample_host", "tg_spec_verify", "tg_sampler_device_status", "tg_sampler_path_counters",
-            "tg_spec_verify_static", "tg_sample_shard_local", "tg_sample_shard_merge", "tg_sampler_profile", "tg_spec_verify_masked",
+            "tg_spec_verify_static", "tg_sample_shard_local", "tg_sample_shard_merge", "tg_sampler_profile", "tg_spec_verify_masked", "tg_sample_sharded",
             "tg_grammar_last_error", "tg_grammar_create", "tg_grammar_destroy",
             "tg_grammar_state_create", "tg_grammar_state_destroy", "tg_grammar_accept_bytes",
             "tg_grammar_kind", "tg_grammar_state_clone",
@@ -91,6 +91,9 @@ def load(path: str = LIB_PATH):
     L.tg_sample_shard_local.restype = i32
     L.tg_sample_shard_merge.argtypes = [vp, vp, i32, i32, i32, vp, vp, vp, vp, vp]
     L.tg_sample_shard_merge.restype = i32
+    L.tg_sample_sharded.argtypes = [vp, vp, i32, i32, i32, vp, i32, i64, i32, vp, vp, vp, i32, vp, i32, vp,
+                                    vp, vp, vp, vp]
+    L.tg_sample_sharded.restype = i32
     L.tg_sampler_profile.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(i32)]
     L.tg_sampler_profile.restype = i32
     L.tg_grammar_last_error.argtypes = []

@@ -5,6 +5,8 @@
 // first growth of the verification statistics buffer.
 #include <cuda_runtime.h>
 
+#include <dlfcn.h>
+
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -108,6 +110,7 @@ struct tg_sampler {
   cudaStream_t stream = nullptr;  // used by tg_sample_host only
   // two-kernel mode: raw candidate lists of up to split_rows rows per launch pair
   DevBuf cand;
+  DevBuf shard_recs;   // tg_sample_sharded: local records, then the gathered ones
   int split_rows = 0;  // 0: single-kernel mode
   // tg_sampler_profile: events around the kernels of the last tg_sample call
   bool profile = false;
@@ -181,6 +184,7 @@ int32_t tg_sampler_destroy(tg_sampler* s) {
     if (s->d_counters) cudaFree(s->d_counters);
     s->stats.release();
     s->cand.release();
+    s->shard_recs.release();
     for (cudaEvent_t ev : s->prof_ev)
       if (ev) cudaEventDestroy(ev);
     for (DevBuf* b : {&s->h_logits, &s->h_params, &s->h_hist, &s->h_hlen, &s->h_mask, &s->h_state,
@@ -361,6 +365,57 @@ int32_t tg_sample_shard_merge(tg_sampler* s, const tg_shard_record* records, int
                             static_cast<cudaStream_t>(stream)>>>(m);
   TG_CUDA(cudaGetLastError());
   return TG_OK;
+}
+
+// ncclAllGather of the NCCL the host process has loaded (the one that made the
+// caller's communicator), found at run time so this library links no NCCL.
+// NCCL's ABI: ncclResult_t (0 = success), ncclUint8 = 1.
+typedef int (*tg_nccl_allgather_fn)(const void*, void*, size_t, int, void*, cudaStream_t);
+
+// Global symbols first, then an NCCL already loaded with local scope (found by
+// its soname; RTLD_NOLOAD never loads a new copy).  A miss is not cached.
+static tg_nccl_allgather_fn nccl_allgather() {
+  static tg_nccl_allgather_fn fn = nullptr;
+  if (fn) return fn;
+  void* sym = dlsym(RTLD_DEFAULT, "ncclAllGather");
+  for (const char* name : {"libnccl.so.2", "libnccl.so"}) {
+    if (sym) break;
+    void* h = dlopen(name, RTLD_LAZY | RTLD_NOLOAD);
+    if (h) sym = dlsym(h, "ncclAllGather");
+  }
+  fn = reinterpret_cast<tg_nccl_allgather_fn>(sym);
+  return fn;
+}
+
+int32_t tg_sample_sharded(tg_sampler* s, void* nccl_comm, int32_t nranks, int32_t vocab_offset,
+                          int32_t full_vocab, const void* logits, int32_t dtype, int64_t row_stride,
+                          int32_t batch, const tg_row_params* params, const int32_t* history,
+                          const int32_t* history_len, int32_t history_stride,
+                          const uint32_t* mask_table, int32_t num_states, const int32_t* state_id,
+                          const float* uniforms, int32_t* out_ids, float* out_probs, void* stream) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (!nccl_comm || nranks <= 0) return fail(TG_ERR_INVALID_ARG, "nccl_comm and nranks > 0 are required");
+  if (batch < 0 || batch > s->max_batch) return fail(TG_ERR_INVALID_ARG, "batch outside [0, max_batch]");
+  if (batch == 0) return TG_OK;
+  if (!out_ids) return fail(TG_ERR_INVALID_ARG, "out_ids is required");
+  const tg_nccl_allgather_fn allgather = nccl_allgather();
+  if (!allgather) return fail(TG_ERR_UNSUPPORTED, "no NCCL library is loaded in this process (ncclAllGather not found)");
+  const size_t rec = sizeof(tg_shard_record) * static_cast<size_t>(batch);
+  {
+    std::lock_guard<std::mutex> lk(s->mu);
+    DeviceGuard g(s->device);
+    TG_CUDA(s->shard_recs.ensure(rec * (1 + static_cast<size_t>(nranks))));
+  }
+  tg_shard_record* local = static_cast<tg_shard_record*>(s->shard_recs.p);
+  tg_shard_record* all = local + batch;
+  int32_t rc = launch_sample(s, vocab_offset, full_vocab, local, logits, dtype, row_stride, batch, params,
+                             history, history_len, history_stride, mask_table, num_states, state_id,
+                             nullptr, nullptr, nullptr, stream);
+  if (rc != TG_OK) return rc;
+  DeviceGuard g(s->device);
+  const int nr = allgather(local, all, rec, 1 /* ncclUint8 */, nccl_comm, static_cast<cudaStream_t>(stream));
+  if (nr != 0) return fail(TG_ERR_CUDA, "ncclAllGather failed (ncclResult_t " + std::to_string(nr) + ")");
+  return tg_sample_shard_merge(s, all, nranks, full_vocab, batch, params, uniforms, out_ids, out_probs, stream);
 }
 
 int32_t tg_sample_host(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_stride,

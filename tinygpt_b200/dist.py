@@ -61,3 +61,45 @@ def sample_vocab_sharded(sampler, logits_shard, params, vocab_offset: int, full_
     ids, probs = sampler.sample_shard_merge(gathered, full_vocab, params, uniforms=uniforms,
                                             out_probs=out_probs)
     return ids, probs
+
+
+class NcclComm:
+    """An NCCL communicator for tg_sample_sharded, made with the NCCL library
+    that torch has loaded (so the library and the communicator agree).  Rank 0's
+    unique id reaches the other ranks through the torch.distributed default
+    group; a single rank needs no process group.  `.ptr` is the ncclComm_t."""
+
+    def __init__(self, rank: int, world: int, device: int):
+        import ctypes
+        import torch
+        torch.cuda.set_device(device)
+        torch.cuda.init()
+        self._nccl = ctypes.CDLL("libnccl.so.2")  # the copy already loaded by torch
+
+        class UniqueId(ctypes.Structure):  # ncclUniqueId, passed by value
+            _fields_ = [("internal", ctypes.c_char * 128)]
+
+        uid = UniqueId()
+        if rank == 0 and self._nccl.ncclGetUniqueId(ctypes.byref(uid)) != 0:
+            raise RuntimeError("ncclGetUniqueId failed")
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.frombuffer(bytearray(bytes(uid)), dtype=torch.uint8).clone()
+            if dist.get_backend() == "nccl":
+                t = t.cuda()
+            dist.broadcast(t, 0)
+            uid = UniqueId.from_buffer_copy(bytes(t.cpu().numpy()))
+        comm = ctypes.c_void_p()
+        self._nccl.ncclCommInitRank.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                                UniqueId, ctypes.c_int]
+        if self._nccl.ncclCommInitRank(ctypes.byref(comm), world, uid, rank) != 0:
+            raise RuntimeError("ncclCommInitRank failed")
+        self.ptr = comm.value
+        self.world = world
+
+    def close(self) -> None:
+        import ctypes
+        if self.ptr:
+            self._nccl.ncclCommDestroy.argtypes = [ctypes.c_void_p]
+            self._nccl.ncclCommDestroy(ctypes.c_void_p(self.ptr))
+            self.ptr = None

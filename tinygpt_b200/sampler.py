@@ -219,6 +219,27 @@ class Sampler:
                                             _ptr(out_probs), _stream_ptr(stream)))
         return out, out_probs
 
+    def sample_sharded(self, nccl_comm, nranks: int, logits, params, vocab_offset: int, full_vocab: int, *,
+                       history=None, history_len=None, mask_table=None, state_id=None, uniforms=None,
+                       out=None, out_probs=None, stream=None):
+        """tg_sample_sharded: this rank's vocab slice of every row, the record
+        all-gather over the NCCL communicator (an ncclComm_t pointer, see
+        tinygpt_b200.dist.NcclComm) and the merge; ids for the whole rows."""
+        B, _ = logits.shape
+        dev = logits.device
+        if isinstance(params, np.ndarray):
+            params = params_to_device(params, dev)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=dev)
+        hstride = history.shape[1] if history is not None else 0
+        nstates = mask_table.shape[0] if mask_table is not None else 0
+        check(self._L.tg_sample_sharded(self._h, ctypes.c_void_p(int(nccl_comm)), nranks, vocab_offset,
+                                        full_vocab, _ptr(logits), _dtype_code(logits), logits.stride(0), B,
+                                        _ptr(params), _ptr(history), _ptr(history_len), hstride,
+                                        _ptr(mask_table), nstates, _ptr(state_id), _ptr(uniforms),
+                                        _ptr(out), _ptr(out_probs), _stream_ptr(stream)))
+        return out, out_probs
+
     def path_counters(self, reset: bool = True) -> dict:
         """Row counts per sampling path since the last reset (see tgsample.h)."""
         buf = (ctypes.c_uint64 * 8)()
