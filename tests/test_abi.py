@@ -39,6 +39,12 @@ def test_abi_version_and_errors_without_device(cuda_lib):
     rc = cuda_lib.tg_spec_verify_static(0, 100, None, None, 7, 1, 1, None, None, None, None, None,
                                         None, None)
     assert rc == _lib.TG_ERR_INVALID_ARG
+    rc = cuda_lib.tg_spec_verify_masked(None, None, None, 0, 1, 1, None, None, None, None, None, 1, None,
+                                        None, None, None)
+    assert rc == _lib.TG_ERR_INVALID_ARG
+    rc = cuda_lib.tg_sample_sharded(None, None, 1, 0, 100, None, 0, 100, 1, None, None, None, 0, None, 0,
+                                    None, None, None, None, None)
+    assert rc == _lib.TG_ERR_INVALID_ARG and b"sampler is NULL" in cuda_lib.tg_last_error_string()
 
 
 def test_row_params_layout():
