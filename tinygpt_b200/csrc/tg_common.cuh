@@ -19,9 +19,8 @@ constexpr double kResidScale = 4503599627370496.0;  // 2^52: scale of residual m
 // (truncation error < 6e-9 relative), then an exact scaling by 2^n done as one
 // or two multiplications by powers of two.  Accuracy < 1 ulp over the normal
 // range (checked against libm in the tests).  Independent of CUDA's expf.
-__device__ __forceinline__ float tg_exp(float x) {
-  if (!(x > -104.0f)) return 0.0f;
-  if (x > 88.0f) return __int_as_float(0x7f800000);
+// The reduction and the polynomial: x = n*ln2 + r, p = e^r.
+__device__ __forceinline__ float tg_exp_poly(float x, int& ni) {
   const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
   float r = __fmaf_rn(n, -0.693145751953125f, x);
   r = __fmaf_rn(n, -1.42860676533018e-06f, r);
@@ -33,7 +32,15 @@ __device__ __forceinline__ float tg_exp(float x) {
   p = __fmaf_rn(p, r, 0.5f);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
-  const int ni = __float2int_rn(n);
+  ni = __float2int_rn(n);
+  return p;
+}
+
+__device__ __forceinline__ float tg_exp(float x) {
+  if (!(x > -104.0f)) return 0.0f;
+  if (x > 88.0f) return __int_as_float(0x7f800000);
+  int ni;
+  float p = tg_exp_poly(x, ni);
   if (ni >= -126) return __fmul_rn(p, __uint_as_float(static_cast<uint32_t>(ni + 127) << 23));
   p = __fmul_rn(p, __uint_as_float(1u << 23));
   return __fmul_rn(p, __uint_as_float(static_cast<uint32_t>(ni + 126 + 127) << 23));
@@ -43,6 +50,17 @@ __device__ __forceinline__ float tg_exp(float x) {
 __device__ __forceinline__ uint64_t qmass(float d) {
   if (!(d >= -32.0f)) return 0ull;
   return __float2ull_rz(__fmul_rn(tg_exp(d), kMassScale));
+}
+
+// qmass(d) for d <= 0 without branches: for -32 <= d <= 0 tg_exp takes its
+// first scaling branch (n >= -47), so the same operations give the same bits;
+// below -32 (or NaN) the select gives 0.
+__device__ __forceinline__ uint64_t qmass_le0(float d) {
+  int ni;
+  const float p = tg_exp_poly(d, ni);
+  const float e = __fmul_rn(p, __uint_as_float((static_cast<uint32_t>(ni) + 127u) << 23));
+  const uint64_t q = __float2ull_rz(__fmul_rn(e, kMassScale));
+  return d >= -32.0f ? q : 0ull;
 }
 
 // Order-preserving 32-bit key of a float (-0 folded onto +0).

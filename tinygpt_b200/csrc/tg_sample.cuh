@@ -67,7 +67,7 @@ static_assert(kCandMax <= kWideMassN, "candidate mass histograms must not overfl
 
 // Diagnostic build only (-DTG_PHASE_TIMING): cycles per phase summed over CTAs.
 #ifdef TG_PHASE_TIMING
-__device__ unsigned long long g_phase_cycles[16];
+__device__ unsigned long long g_phase_cycles[32];
 #endif
 struct PhaseClock {
   long long last = 0;
@@ -116,6 +116,9 @@ struct SampleArgs {
   int32_t* cand_gid;
   int32_t* cand_gn;
   float* cand_gth;
+  // warp finisher: rows it left for sample_list_kernel, and their count
+  int32_t* fb_rows;
+  int32_t* fb_count;
 };
 
 // History hash in shared memory: key = token id (-1 empty); val = count, then
@@ -1064,15 +1067,14 @@ __device__ void shard_emit(const Src& src, const tg_row_params& p, int V, int mo
 
 // kStream: the streaming half of the two-kernel mode (threshold, streaming
 // pass, raw candidates to global memory); no history, no selection code.
-template <int DT, bool kStream = false, int NT = kSampleNT>
-__global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerSm * kSampleNT / NT > 0 ? kMinCtasPerSm * kSampleNT / NT : 1)) sample_kernel(SampleArgs a) {
+template <int DT, bool kStream, int NT>
+__device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
   using E = Elt<DT>;
   constexpr int EPV = E::kEPV;
   constexpr int SV = kSampleVecs;
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ BlockScratch sm;
   __shared__ uint32_t bloom[128];
-  const int b = blockIdx.x;
   const int t = threadIdx.x;
   const int moff = a.vocab_offset;  // global id of this shard's element 0
   const int V = a.vocab;
@@ -1615,6 +1617,25 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
   if (t == 0) {
     a.out_ids[b] = out_id;
     if (a.out_probs) a.out_probs[b] = out_prob;
+  }
+}
+
+template <int DT, bool kStream = false, int NT = kSampleNT>
+__global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerSm * kSampleNT / NT > 0 ? kMinCtasPerSm * kSampleNT / NT : 1)) sample_kernel(SampleArgs a) {
+  if constexpr (kStream) {  // the fallback list of this launch pair starts empty
+    if (a.fb_count && blockIdx.x == 0 && threadIdx.x == 0) *a.fb_count = 0;
+  }
+  sample_row<DT, kStream, NT>(a, blockIdx.x);
+}
+
+// The rows the warp finisher left (a.fb_rows[0 .. *a.fb_count)), one CTA at a
+// time per row, over a grid of at most a few CTAs per SM.
+template <int DT>
+__global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_list_kernel(SampleArgs a) {
+  const int n = *a.fb_count;
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    __syncthreads();  // shared state of the previous row is dead
+    sample_row<DT, false, kSampleNT>(a, a.fb_rows[i]);
   }
 }
 

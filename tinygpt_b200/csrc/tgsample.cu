@@ -15,6 +15,7 @@
 
 #include "../../include/tgsample.h"
 #include "tg_sample.cuh"
+#include "tg_finish_warp.cuh"
 #include "tg_spec.cuh"
 
 namespace {
@@ -120,6 +121,12 @@ struct tg_sampler {
 };
 
 namespace {
+// An environment switch set to "0" turns the feature off (diagnostics).
+bool getenv_off(const char* name) {
+  const char* v = getenv(name);
+  return v && v[0] == '0';
+}
+
 // Rows per streaming / finishing launch pair (bounds the candidate buffer:
 // kCandMax * 8 + 8 bytes per row).
 constexpr int kSplitRows = 4096;
@@ -157,6 +164,10 @@ int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_s
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tg::sample_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tg::sample_list_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tg::sample_list_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tg::sample_kernel<0, false, tg::kWideNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tg::sample_kernel<1, false, tg::kWideNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
@@ -166,7 +177,11 @@ int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_s
   if (e == cudaSuccess && vocab > tg::kCandMax && max_batch >= kSplitMinBatch &&
       !(split_env && split_env[0] == '0')) {
     s->split_rows = max_batch < kSplitRows ? max_batch : kSplitRows;
-    e = s->cand.ensure(static_cast<size_t>(s->split_rows) * (static_cast<size_t>(tg::kCandMax) * 8 + 8));
+    // per row: the list (value, id), its length and theta, a fallback-list slot; one count
+    e = s->cand.ensure(static_cast<size_t>(s->split_rows) * (static_cast<size_t>(tg::kCandMax) * 8 + 12) + 16);
+  }
+  if (e == cudaSuccess && s->split_rows) {
+    e = cudaFuncSetAttribute(tg::finish_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
   }
   if (e != cudaSuccess) {
     tg_sampler_destroy(s);
@@ -284,6 +299,15 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
   a.cand_gid = reinterpret_cast<int32_t*>(cb + static_cast<size_t>(R) * tg::kCandMax * 4);
   a.cand_gn = reinterpret_cast<int32_t*>(cb + static_cast<size_t>(R) * tg::kCandMax * 8);
   a.cand_gth = reinterpret_cast<float*>(cb + static_cast<size_t>(R) * (tg::kCandMax * 8 + 4));
+  // the warp finisher takes the rows of a call whose history hash fits a warp's
+  // share of shared memory; the vocab-sharded mode keeps the CTA finisher
+  const bool warp_fin = !shard_out && a.ht_log2 <= 11 && !getenv_off("TG_WARP_FINISH");
+  if (warp_fin) {
+    a.fb_rows = reinterpret_cast<int32_t*>(cb + static_cast<size_t>(R) * (tg::kCandMax * 8 + 8));
+    a.fb_count = reinterpret_cast<int32_t*>(cb + static_cast<size_t>(R) * (tg::kCandMax * 8 + 12));
+  }
+  int nsm = 148;
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, s->device);
   const size_t ring_smem = static_cast<size_t>(tg::kSampleNT / 32) * tg::kRing * 20;
   const int64_t es = dtype == TG_DTYPE_F32 ? 4 : 2;
   for (int32_t r0 = 0; r0 < batch; r0 += R) {
@@ -305,10 +329,23 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
     else
       tg::sample_kernel<1, true><<<n, tg::kSampleNT, ring_smem, st>>>(c);
     if (mark) TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
-    if (dtype == TG_DTYPE_F32)
+    if (warp_fin) {  // a warp per row, then the rows it left on CTAs
+      // one CTA per SM: ceil(n / SMs) warps (rows) each, at most kWfMaxWarps
+      int wpc = (n + nsm - 1) / nsm;
+      wpc = wpc < 1 ? 1 : (wpc > tg::kWfMaxWarps ? tg::kWfMaxWarps : wpc);
+      const size_t wsb = static_cast<size_t>(wpc) * tg::warp_fin_bytes(a.ht_log2);
+      const int pool = static_cast<int>((static_cast<size_t>(tg::kWfSmem) - wsb) / 8);
+      tg::finish_warp_kernel<<<(n + wpc - 1) / wpc, wpc * 32, tg::kWfSmem, st>>>(c, pool);
+      const int g = n < nsm * tg::kMinCtasPerSm ? n : nsm * tg::kMinCtasPerSm;
+      if (dtype == TG_DTYPE_F32)
+        tg::sample_list_kernel<0><<<g, tg::kSampleNT, smem, st>>>(c);
+      else
+        tg::sample_list_kernel<1><<<g, tg::kSampleNT, smem, st>>>(c);
+    } else if (dtype == TG_DTYPE_F32) {
       tg::sample_kernel<0><<<n, tg::kSampleNT, smem, st>>>(c);
-    else
+    } else {
       tg::sample_kernel<1><<<n, tg::kSampleNT, smem, st>>>(c);
+    }
     TG_CUDA(cudaGetLastError());
   }
   if (s->profile) {
@@ -576,9 +613,9 @@ int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_
 #ifdef TG_PHASE_TIMING
 int32_t tg_debug_phase_cycles(uint64_t* out, int32_t reset) {
   TG_CUDA(cudaDeviceSynchronize());
-  TG_CUDA(cudaMemcpyFromSymbol(out, tg::g_phase_cycles, sizeof(uint64_t) * 16));
+  TG_CUDA(cudaMemcpyFromSymbol(out, tg::g_phase_cycles, sizeof(uint64_t) * 32));
   if (reset) {
-    static const uint64_t z[16] = {};
+    static const uint64_t z[32] = {};
     TG_CUDA(cudaMemcpyToSymbol(tg::g_phase_cycles, z, sizeof(z)));
   }
   return TG_OK;
