@@ -31,27 +31,58 @@
 
 namespace tg {
 
-constexpr int kWfMaxWarps = 16;      // rows (warps) per CTA at most
-constexpr int kWfMaxNT = kWfMaxWarps * 32;
+constexpr int kWfMaxWarps = 16;      // rows per CTA at most
+constexpr int kWfGroupWarps = 28;    // warps per CTA at most (<= 73 registers per thread)
+constexpr int kWfMaxNT = kWfGroupWarps * 32;
 constexpr int kWfSmem = 227 * 1024 - 256;  // dynamic shared memory of a CTA (static: 64 B)
 constexpr int kWfBins = 256;         // histogram bins of one selection round
 constexpr int kWfMaxHist = 1024;     // longest history served (hash of 2048 slots)
 constexpr int kWfBloomWords = 256;   // 8192-bit Bloom filter of the history ids
 
-// Per-warp selection scratch: bin weights and the small list of a crossing bin.
-struct WarpSel {
+// A group of G warps that finishes one row.  G == 1 synchronizes with
+// __syncwarp; larger groups with the named barrier id + 1 (ids 1..15; id 0 is
+// __syncthreads').
+template <int G>
+struct Grp {
+  static constexpr int NT = 32 * G;
+  int id;    // group index in the CTA
+  int gt;    // thread index in the group
+  int gw;    // warp index in the group
+  int lane;
+  __device__ __forceinline__ void sync() const {
+    if constexpr (G == 1) {
+      __syncwarp();
+    } else {
+      asm volatile("bar.sync %0, %1;" ::"r"(id + 1), "n"(NT) : "memory");
+    }
+  }
+};
+
+// Per-group selection scratch: bin weights, the small list of a crossing bin,
+// and the group's reduction slots.
+struct GrpSel {
   unsigned int hl[3][kWfBins];  // 15-bit limbs of the bin weights (masses <= 2^44)
   unsigned long long sk[32];
   unsigned long long sw[32];
+  unsigned long long ru[4];     // per-warp partials
+  unsigned long long rv[4];
+  float rf[4];
+  float rg[4];
+  int ri[4];
   int cnt;
-  int pad[3];
+  int bin;
+  unsigned long long bb;
+  unsigned long long res_key;
+  unsigned long long res_w;
+  unsigned long long res_before;
+  int res;                      // 0: not reached, 1: resolved, 2: narrow
 };
 
-// Per-warp scratch: the Bloom filter, then the history hash (penalty pass
+// Per-group scratch: the Bloom filter, then the history hash (penalty pass
 // only) sharing its bytes with the selection scratch.
-__host__ __device__ __forceinline__ size_t warp_fin_bytes(int ht_log2) {
+__host__ __device__ __forceinline__ size_t grp_fin_bytes(int ht_log2) {
   const size_t h = ht_log2 ? (size_t(4) << ht_log2) : 0;
-  const size_t s = sizeof(WarpSel);
+  const size_t s = sizeof(GrpSel);
   return 4 * kWfBloomWords + (((h > s ? h : s) + 15) & ~size_t(15));
 }
 
@@ -66,6 +97,21 @@ __device__ __forceinline__ unsigned long long warp_incl_scan(unsigned long long 
   return v;
 }
 
+// Group sum of a u64 (every thread gets it).
+template <int G>
+__device__ __forceinline__ unsigned long long grp_sum(const Grp<G>& g, GrpSel& ws, unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  if constexpr (G == 1) return v;
+  if (g.lane == 0) ws.ru[g.gw] = v;
+  g.sync();
+  unsigned long long r = 0;
+#pragma unroll
+  for (int i = 0; i < G; i++) r += ws.ru[i];
+  g.sync();
+  return r;
+}
+
 // Shift that maps key - lo, for keys in [lo, lo + width], onto 256 bins.
 template <class K>
 __device__ __forceinline__ int sel_shift(K width) {
@@ -74,18 +120,17 @@ __device__ __forceinline__ int sel_shift(K width) {
   return bits > 8 ? bits - 8 : 0;
 }
 
-template <bool kMass>
-__device__ __forceinline__ void sel_zero(WarpSel& ws) {
-  const int lane = threadIdx.x & 31;
+template <bool kMass, int G>
+__device__ __forceinline__ void sel_zero(const Grp<G>& g, GrpSel& ws) {
 #pragma unroll
-  for (int j = 0; j < kWfBins / 32; j++) {
-    ws.hl[0][lane + 32 * j] = 0u;
-    if (kMass) { ws.hl[1][lane + 32 * j] = 0u; ws.hl[2][lane + 32 * j] = 0u; }
+  for (int j = 0; j < kWfBins / (32 * G); j++) {
+    ws.hl[0][g.gt + 32 * G * j] = 0u;
+    if (kMass) { ws.hl[1][g.gt + 32 * G * j] = 0u; ws.hl[2][g.gt + 32 * G * j] = 0u; }
   }
 }
 
 template <bool kMass>
-__device__ __forceinline__ void sel_put(WarpSel& ws, int bn, unsigned long long w) {
+__device__ __forceinline__ void sel_put(GrpSel& ws, int bn, unsigned long long w) {
   if (kMass) {
     atomicAdd(&ws.hl[0][bn], static_cast<unsigned>(w & 0x7fffu));
     atomicAdd(&ws.hl[1][bn], static_cast<unsigned>((w >> 15) & 0x7fffu));
@@ -96,64 +141,65 @@ __device__ __forceinline__ void sel_put(WarpSel& ws, int bn, unsigned long long 
 }
 
 // Weighted selection in ascending key order over the elements that iter(f)
-// yields (f(key, value) per element, lanes striding; wt(key, value) gives the
-// weight, 0 = not taking part; weights are counts when !kMass, else masses
-// <= 2^44 summed in 15-bit limbs): the first element at which
-// reached(weight of every element up to and including it) holds.
+// yields (f(key, value) per element, the group's threads striding; wt(key,
+// value) gives the weight, 0 = not taking part; weights are counts when
+// !kMass, else masses <= 2^44 summed in 15-bit limbs): the first element at
+// which reached(weight of every element up to and including it) holds.
 // Each round histograms the keys of [lo, hi] into 256 bins (bin = (key - lo) >>
-// sh), finds the crossing bin by a warp scan, then either resolves it exactly
-// (<= 32 members, sorted in registers; or all members share one key) or
-// narrows [lo, hi] to the members' key range, which is at least 8 bits
+// sh); warp 0 finds the crossing bin by a scan; then the bin is resolved
+// exactly (<= 32 members, sorted in warp 0's registers; or all members share
+// one key) or [lo, hi] narrows to the members' key range, at least 8 bits
 // narrower.  With prefilled, the caller has already put the elements of round
-// 0 into the histogram (sel_zero, then sel_put at bin (key - lo) >> sel_shift(hi - lo)).
+// 0 into the histogram (sel_zero, then sel_put at bin (key - lo) >>
+// sel_shift(hi - lo)) and synchronized the group.
 // Outputs: the key, the weight strictly before it in key order, and its weight
 // (when it is the only member with that key).  Returns false if reached() never
 // holds (the caller falls back).
-template <bool kMass, class K, class Iter, class Wt, class Reached>
-__device__ bool warp_select(Iter iter, Wt wt, K lo, K hi, bool prefilled, Reached reached, WarpSel& ws,
-                            K& key_out, unsigned long long& before_out, unsigned long long& w_out) {
-  const int lane = threadIdx.x & 31;
+template <bool kMass, class K, int G, class Iter, class Wt, class Reached>
+__device__ bool grp_select(const Grp<G>& g, Iter iter, Wt wt, K lo, K hi, bool prefilled, Reached reached,
+                           GrpSel& ws, K& key_out, unsigned long long& before_out, unsigned long long& w_out) {
+  const int lane = g.lane;
   unsigned long long before = 0;
   for (int round = 0; round <= 2 * static_cast<int>(sizeof(K)); round++) {
     const int sh = sel_shift<K>(hi - lo);
     if (!(prefilled && round == 0)) {
-      sel_zero<kMass>(ws);
-      __syncwarp();
+      sel_zero<kMass>(g, ws);
+      g.sync();
       iter([&](K key, float v) {
         if (key < lo || key > hi) return;
         const unsigned long long w = wt(key, v);
         if (w) sel_put<kMass>(ws, static_cast<int>((key - lo) >> sh), w);
       });
+      g.sync();
     }
-    __syncwarp();
-    unsigned long long c[kWfBins / 32];
-    unsigned long long loc = 0;
-#pragma unroll
-    for (int j = 0; j < kWfBins / 32; j++) {
-      const int bn = lane * (kWfBins / 32) + j;
-      c[j] = kMass ? static_cast<unsigned long long>(ws.hl[0][bn]) + (static_cast<unsigned long long>(ws.hl[1][bn]) << 15) +
-                         (static_cast<unsigned long long>(ws.hl[2][bn]) << 30)
-                   : static_cast<unsigned long long>(ws.hl[0][bn]);
-      loc += c[j];
-    }
-    const unsigned long long incl = warp_incl_scan(loc);
-    const unsigned bal = __ballot_sync(kFull, reached(before + incl));
-    if (!bal) return false;
-    const int L = __ffs(bal) - 1;
-    int bin = 0;
-    unsigned long long bb = 0;
-    if (lane == L) {
-      unsigned long long cc = before + incl - loc;
+    if (g.gw == 0) {  // warp 0: the crossing bin
+      unsigned long long c[kWfBins / 32];
+      unsigned long long loc = 0;
 #pragma unroll
       for (int j = 0; j < kWfBins / 32; j++) {
-        if (reached(cc + c[j])) { bin = lane * (kWfBins / 32) + j; bb = cc; break; }
-        cc += c[j];
+        const int bn = lane * (kWfBins / 32) + j;
+        c[j] = kMass ? static_cast<unsigned long long>(ws.hl[0][bn]) + (static_cast<unsigned long long>(ws.hl[1][bn]) << 15) +
+                           (static_cast<unsigned long long>(ws.hl[2][bn]) << 30)
+                     : static_cast<unsigned long long>(ws.hl[0][bn]);
+        loc += c[j];
+      }
+      const unsigned long long incl = warp_incl_scan(loc);
+      const unsigned bal = __ballot_sync(kFull, reached(before + incl));
+      if (lane == 0) { ws.bin = -1; ws.cnt = 0; }
+      __syncwarp();
+      if (bal && lane == __ffs(bal) - 1) {
+        unsigned long long cc = before + incl - loc;
+#pragma unroll
+        for (int j = 0; j < kWfBins / 32; j++) {
+          if (reached(cc + c[j])) { ws.bin = lane * (kWfBins / 32) + j; ws.bb = cc; break; }
+          cc += c[j];
+        }
       }
     }
-    bin = __shfl_sync(kFull, bin, L);
-    bb = __shfl_sync(kFull, bb, L);
-    if (lane == 0) ws.cnt = 0;
-    __syncwarp();
+    g.sync();
+    const int bin = ws.bin;
+    const unsigned long long bb = ws.bb;
+    if (bin < 0) return false;
     // members of the crossing bin: key range, count, the first 32
     const K blo = lo + (static_cast<K>(bin) << sh);
     const K span = (K(1) << sh) - K(1);
@@ -175,45 +221,66 @@ __device__ bool warp_select(Iter iter, Wt wt, K lo, K hi, bool prefilled, Reache
       kmin = x < kmin ? x : kmin;
       kmax = y > kmax ? y : kmax;
     }
-    __syncwarp();
+    if constexpr (G > 1) {
+      if (lane == 0) { ws.ru[g.gw] = static_cast<unsigned long long>(kmin); ws.rv[g.gw] = static_cast<unsigned long long>(kmax); }
+    }
+    g.sync();
+    if constexpr (G > 1) {
+#pragma unroll
+      for (int i = 0; i < G; i++) {
+        const K x = static_cast<K>(ws.ru[i]), y = static_cast<K>(ws.rv[i]);
+        kmin = x < kmin ? x : kmin;
+        kmax = y > kmax ? y : kmax;
+      }
+    }
     const int n = ws.cnt;
     if (n == 0) return false;
     if (kmin == kmax) {  // one key: the crossing element has it
-      const unsigned long long w = (n == 1 && lane == 0) ? ws.sw[0] : 0ull;
-      w_out = __shfl_sync(kFull, w, 0);
+      w_out = n == 1 ? ws.sw[0] : 0ull;
       key_out = kmin;
       before_out = bb;
-      __syncwarp();
+      g.sync();
       return true;
     }
-    if (n <= 32) {  // sort the members by key, scan their weights
-      unsigned long long k = lane < n ? ws.sk[lane] : ~0ull;
-      unsigned long long x = lane < n ? ws.sw[lane] : 0ull;
+    if (n <= 32) {  // warp 0 sorts the members by key and scans their weights
+      if (g.gw == 0) {
+        unsigned long long k = lane < n ? ws.sk[lane] : ~0ull;
+        unsigned long long x = lane < n ? ws.sw[lane] : 0ull;
 #pragma unroll
-      for (int size = 2; size <= 32; size <<= 1) {
+        for (int size = 2; size <= 32; size <<= 1) {
 #pragma unroll
-        for (int j = size >> 1; j > 0; j >>= 1) {
-          const unsigned long long ok = __shfl_xor_sync(kFull, k, j);
-          const unsigned long long ox = __shfl_xor_sync(kFull, x, j);
-          const bool up = (lane & size) == 0;
-          const bool lower = (lane & j) == 0;
-          const bool take = (lower == up) ? (ok < k) : (ok > k);
-          if (take) { k = ok; x = ox; }
+          for (int j = size >> 1; j > 0; j >>= 1) {
+            const unsigned long long ok = __shfl_xor_sync(kFull, k, j);
+            const unsigned long long ox = __shfl_xor_sync(kFull, x, j);
+            const bool up = (lane & size) == 0;
+            const bool lower = (lane & j) == 0;
+            const bool take = (lower == up) ? (ok < k) : (ok > k);
+            if (take) { k = ok; x = ox; }
+          }
+        }
+        const unsigned long long inc = warp_incl_scan(x);
+        const unsigned hit = __ballot_sync(kFull, lane < n && reached(bb + inc));
+        if (lane == 0) ws.res = 0;
+        __syncwarp();
+        if (hit && lane == __ffs(hit) - 1) {
+          ws.res = 1;
+          ws.res_key = k;
+          ws.res_w = x;
+          ws.res_before = bb + inc - x;
         }
       }
-      const unsigned long long inc = warp_incl_scan(x);
-      const unsigned hit = __ballot_sync(kFull, lane < n && reached(bb + inc));
-      __syncwarp();
-      if (!hit) return false;
-      const int src = __ffs(hit) - 1;
-      key_out = static_cast<K>(__shfl_sync(kFull, k, src));
-      w_out = __shfl_sync(kFull, x, src);
-      before_out = bb + __shfl_sync(kFull, inc, src) - w_out;
-      return true;
+      g.sync();
+      const bool ok = ws.res == 1;
+      key_out = static_cast<K>(ws.res_key);
+      w_out = ws.res_w;
+      before_out = ws.res_before;
+      g.sync();
+      return ok;
     }
     lo = kmin;
     hi = kmax;
     before = bb;
+    g.sync();
   }
   return false;
 }
@@ -255,11 +322,17 @@ __device__ __forceinline__ int warp_row_need(const SampleArgs& a, int b) {
   return (greedy || topk) ? n : 0;
 }
 
-// One warp finishes row b over its list staged in ly / lid (this row's share
-// of the pool, null when the pool had no room).  Returns false when the row is
-// left for the fallback kernel; the global list is only read.
-__device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scratch, float* ly, int* lid) {
-  const int lane = threadIdx.x & 31;
+// A group of G warps finishes row b over its list staged in ly / lid (this
+// row's share of the pool, null when the pool had no room).  Returns false
+// when the row is left for the fallback kernel; the global list is only read.
+// Element i of the list belongs to warp (i / 32) % G; after the compaction each
+// warp keeps its survivors in its own slots, in place (slot(j) below), so no
+// cross-warp prefix is needed.
+template <int G>
+__device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsigned char* scratch, float* ly,
+                               int* lid) {
+  constexpr int NT = 32 * G;
+  const int lane = g.lane, gt = g.gt;
   if (ly == nullptr) return false;
   const int n = a.cand_gn[b];
   const tg_row_params p = a.params[b];
@@ -280,25 +353,25 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
 
   uint32_t* bloom = reinterpret_cast<uint32_t*>(scratch);
   uint32_t* hash = bloom + kWfBloomWords;
-  WarpSel& ws = *reinterpret_cast<WarpSel*>(hash);
+  GrpSel& ws = *reinterpret_cast<GrpSel*>(hash);
   WarpClock wc;
   wc.mark(0);
   const float* gy = a.cand_gy + static_cast<int64_t>(b) * kCandMax;
   const int* gid = a.cand_gid + static_cast<int64_t>(b) * kCandMax;
 
-  // stage the list: 16 loads in flight per lane, straight to shared memory
+  // stage the list: 16 loads in flight per thread, straight to shared memory
   constexpr int LU = 16;
-  for (int base = lane; base < n; base += 32 * LU) {
+  for (int base = gt; base < n; base += NT * LU) {
     float yv[LU];
     int iv[LU];
 #pragma unroll
     for (int q = 0; q < LU; q++) {
-      const int i = base + 32 * q;
+      const int i = base + NT * q;
       if (i < n) { yv[q] = __ldcg(gy + i); iv[q] = __ldcg(gid + i); }
     }
 #pragma unroll
     for (int q = 0; q < LU; q++) {
-      const int i = base + 32 * q;
+      const int i = base + NT * q;
       if (i < n) { ly[i] = yv[q]; lid[i] = iv[q]; }
     }
   }
@@ -306,16 +379,15 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
   // (a) history -> hash of distinct ids with counts, and a Bloom filter of them
   const int hmask = need_hist ? (1 << a.ht_log2) - 1 : 0;
   if (need_hist) {
-    for (int i = lane; i <= hmask; i += 32) hash[i] = 0u;
-#pragma unroll
-    for (int j = 0; j < kWfBloomWords / 32; j++) bloom[lane + 32 * j] = 0u;
-    __syncwarp();
+    for (int i = gt; i <= hmask; i += NT) hash[i] = 0u;
+    for (int i = gt; i < kWfBloomWords; i += NT) bloom[i] = 0u;
+    g.sync();
     const int32_t* h = a.history + static_cast<int64_t>(b) * a.history_stride;
-    constexpr int HU = 16;
-    for (int base = lane; base < hlen; base += 32 * HU) {
+    constexpr int HU = 8;
+    for (int base = gt; base < hlen; base += NT * HU) {
       int ids[HU];
 #pragma unroll
-      for (int q = 0; q < HU; q++) ids[q] = base + 32 * q < hlen ? __ldg(h + base + 32 * q) : -1;
+      for (int q = 0; q < HU; q++) ids[q] = base + NT * q < hlen ? __ldg(h + base + NT * q) : -1;
 #pragma unroll 1
       for (int q = 0; q < HU; q++) {
         int id = ids[0];
@@ -337,7 +409,7 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
       }
     }
   }
-  __syncwarp();
+  g.sync();
   wc.mark(0);  // 16: staging and hash build
   auto count_of = [&](int id) {
     const uint32_t bit = wf_bloom_bit(id);
@@ -357,7 +429,7 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
   float ymax = neg_inf(), nymin = neg_inf();
   int amax = 0x7fffffff;
 #pragma unroll 2
-  for (int i = lane; i < n; i += 32) {
+  for (int i = gt; i < n; i += NT) {
     float y = ly[i];
     const int id = lid[i];
     if (need_hist) {
@@ -385,13 +457,30 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
     if (oy > ymax || (oy == ymax && oi < amax)) { ymax = oy; amax = oi; }
     nymin = fmaxf(nymin, __shfl_xor_sync(kFull, nymin, o));
   }
-  __syncwarp();  // the hash is dead from here; its bytes become ws
+  g.sync();  // the hash is dead from here; its bytes become ws
+  if constexpr (G > 1) {
+    if (lane == 0) { ws.ru[g.gw] = cnt; ws.rf[g.gw] = ymax; ws.ri[g.gw] = amax; ws.rg[g.gw] = nymin; }
+    g.sync();
+    cnt = 0;
+    ymax = neg_inf();
+    nymin = neg_inf();
+    amax = 0x7fffffff;
+#pragma unroll
+    for (int w = 0; w < G; w++) {
+      cnt += static_cast<unsigned int>(ws.ru[w]);
+      const float oy = ws.rf[w];
+      const int oi = ws.ri[w];
+      if (oy > ymax || (oy == ymax && oi < amax)) { ymax = oy; amax = oi; }
+      nymin = fmaxf(nymin, ws.rg[w]);
+    }
+    g.sync();
+  }
   wc.mark(1);  // 17: penalty pass
 
   const unsigned int need = greedy ? 1u : static_cast<unsigned int>(p.top_k);
   if (cnt < need) return false;
   if (greedy) {
-    if (lane == 0) {
+    if (gt == 0) {
       a.out_ids[b] = amax;
       if (a.out_probs) a.out_probs[b] = 1.0f;
     }
@@ -403,10 +492,11 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
   uint32_t kk;
   unsigned long long kb, kw;
   const unsigned int k = static_cast<unsigned int>(p.top_k);
-  const bool okk = warp_select<false, uint32_t>(
+  const bool okk = grp_select<false, uint32_t>(
+      g,
       [&](auto&& f) {
 #pragma unroll 2
-        for (int i = lane; i < n; i += 32) {
+        for (int i = gt; i < n; i += NT) {
           const float y = ly[i];
           if (y >= theta) f(~fkey(y), y);
         }
@@ -420,8 +510,9 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
   const float below = key2f(fkey(theta) - 1u);  // every absent value is <= below
   if (__fdiv_rn(below, T) >= sk) return false;
 
-  // (b) survivors compacted in place (tempered value, id), their mass total,
-  // and the first top-p histogram round over their (s desc, id asc) keys
+  // (b) survivors compacted in place (tempered value, id) per warp, their
+  // mass total, and the first top-p histogram round over their (s desc, id
+  // asc) keys
   const float smax = __fdiv_rn(ymax, T);
   const bool toppon = p.top_p < 1.0f;
   const unsigned long long plo = static_cast<unsigned long long>(~fkey(smax)) << 32;
@@ -430,17 +521,18 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
   auto pkey = [](float sv, int id) {
     return (static_cast<unsigned long long>(~fkey(sv)) << 32) | static_cast<uint32_t>(id);
   };
-  if (toppon) sel_zero<true>(ws);
-  __syncwarp();
+  if (toppon) sel_zero<true>(g, ws);
+  g.sync();
+  auto slot = [&](int j) { return (j >> 5) * NT + g.gw * 32 + (j & 31); };
   const unsigned lt = (1u << lane) - 1u;
-  int m = 0;
+  int m = 0;  // this warp's survivors
   unsigned long long Q = 0;
 #pragma unroll 1
-  for (int base = 0; base < n; base += 32) {
-    const int i = base + lane;
+  for (int base = 0; base < n; base += NT) {
+    const int i = base + g.gw * 32 + lane;
     const float y = i < n ? ly[i] : neg_inf();
     const int id = i < n ? lid[i] : -1;
-    __syncwarp();  // writes go only below the elements loaded
+    __syncwarp();  // writes go only to this warp's slots at or below those loaded
     float sv = 0.0f;
     bool keep = y >= theta && y > neg_inf();
     if (keep) {
@@ -454,15 +546,14 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
     }
     const unsigned bal = __ballot_sync(kFull, keep);
     if (keep) {
-      const int pos = m + __popc(bal & lt);
+      const int pos = slot(m + __popc(bal & lt));
       ly[pos] = sv;
       lid[pos] = id;
     }
     m += __popc(bal);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) Q += __shfl_xor_sync(kFull, Q, o);
   __syncwarp();
+  Q = grp_sum(g, ws, Q);  // its barriers also publish the top-p histogram
   wc.mark(3);  // 19: compaction and Q
 
   auto mass = [&](float sv) { return qmass_le0(__fsub_rn(sv, smax)); };
@@ -474,12 +565,14 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
     const double tau = __dmul_rn(static_cast<double>(p.top_p), __ull2double_rn(Q));
     if (tau > 0.0) {
       unsigned long long ck, cb, cw;
-      const bool ok = warp_select<true, unsigned long long>(
+      const bool ok = grp_select<true, unsigned long long>(
+          g,
           [&](auto&& f) {
 #pragma unroll 2
             for (int j = lane; j < m; j += 32) {
-              const float sv = ly[j];
-              f(pkey(sv, lid[j]), sv);
+              const int i = slot(j);
+              const float sv = ly[i];
+              f(pkey(sv, lid[i]), sv);
             }
           },
           [&](unsigned long long, float sv) { return mass(sv); }, plo, phi, true,
@@ -489,12 +582,21 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
       cut_id = static_cast<int>(static_cast<uint32_t>(ck));
     } else {  // top_p <= 0: the single top element (smallest id among the maxima)
       cut_key = fkey(smax);
-      int best = 0x7fffffff;
-      for (int j = lane; j < m; j += 32)
-        if (fkey(ly[j]) == cut_key) best = min(best, lid[j]);
+      unsigned long long best = 0;  // max of ~id
+      for (int j = lane; j < m; j += 32) {
+        const int i = slot(j);
+        if (fkey(ly[i]) == cut_key) best = max(best, static_cast<unsigned long long>(~static_cast<uint32_t>(lid[i])));
+      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(kFull, best, o));
-      cut_id = best;
+      for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(kFull, best, o));
+      if constexpr (G > 1) {
+        if (lane == 0) ws.ru[g.gw] = best;
+        g.sync();
+#pragma unroll
+        for (int w = 0; w < G; w++) best = max(best, ws.ru[w]);
+        g.sync();
+      }
+      cut_id = static_cast<int>(~static_cast<uint32_t>(best));
     }
   }
   wc.mark(4);  // 20: top-p
@@ -511,18 +613,18 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
   };
   // kept mass S, and the first draw histogram round over ids
   const int dsh = sel_shift<uint32_t>(static_cast<uint32_t>(V - 1));
-  sel_zero<true>(ws);
-  __syncwarp();
+  sel_zero<true>(g, ws);
+  g.sync();
   unsigned long long S = 0;
 #pragma unroll 2
   for (int j = lane; j < m; j += 32) {
-    const int id = lid[j];
-    const unsigned long long q = kept_mass(ly[j], id);
+    const int i = slot(j);
+    const int id = lid[i];
+    const unsigned long long q = kept_mass(ly[i], id);
     S += q;
     if (q) sel_put<true>(ws, id >> dsh, q);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(kFull, S, o);
+  S = grp_sum(g, ws, S);
   if (S == 0) return false;
   wc.mark(5);  // 21: kept mass S
 
@@ -530,45 +632,51 @@ __device__ bool warp_finish_row(const SampleArgs& a, int b, unsigned char* scrat
   const unsigned long long r = draw_point(a.uniforms ? a.uniforms[b] : 0.0f, S);
   uint32_t pk;
   unsigned long long pb, pw;
-  const bool okd = warp_select<true, uint32_t>(
+  const bool okd = grp_select<true, uint32_t>(
+      g,
       [&](auto&& f) {
 #pragma unroll 2
-        for (int j = lane; j < m; j += 32) f(static_cast<uint32_t>(lid[j]), ly[j]);
+        for (int j = lane; j < m; j += 32) {
+          const int i = slot(j);
+          f(static_cast<uint32_t>(lid[i]), ly[i]);
+        }
       },
       [&](uint32_t id, float sv) { return kept_mass(sv, static_cast<int>(id)); }, 0u,
       static_cast<uint32_t>(V - 1), true, [&](unsigned long long c) { return c > r; }, ws, pk, pb, pw);
   if (!okd) return false;
   wc.mark(6);  // 22: draw
-  if (lane == 0) {
+  if (gt == 0) {
     a.out_ids[b] = static_cast<int>(pk);
     if (a.out_probs) a.out_probs[b] = __double2float_rn(__ddiv_rn(__ull2double_rn(pw), __ull2double_rn(S)));
   }
   return true;
 }
 
-// One CTA per SM, one warp per row (blockDim.x / 32 rows per CTA).  The
-// dynamic shared memory holds each warp's scratch, then a pool that the CTA's
-// rows share for their staged lists (a row beyond the pool goes to the
-// fallback list).  Rows a warp does not finish go to the fallback list.
+// One CTA per SM, one group of G warps per row (blockDim.x / (32 G) rows per
+// CTA).  The dynamic shared memory holds each group's scratch, then a pool that
+// the CTA's rows share for their staged lists (a row beyond the pool goes to
+// the fallback list).  Rows a group does not finish go to the fallback list.
+template <int G>
 __global__ void __launch_bounds__(kWfMaxNT, 1) finish_warp_kernel(SampleArgs a, int pool_entries) {
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ int needs[kWfMaxWarps];
-  const int W = blockDim.x >> 5;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.x * W + warp;
-  if (lane == 0) needs[warp] = b < a.batch ? warp_row_need(a, b) : 0;
+  const int R = blockDim.x / (32 * G);  // rows of this CTA
+  const Grp<G> g{static_cast<int>(threadIdx.x) / (32 * G), static_cast<int>(threadIdx.x) % (32 * G),
+                 (static_cast<int>(threadIdx.x) % (32 * G)) >> 5, static_cast<int>(threadIdx.x) & 31};
+  const int b = blockIdx.x * R + g.id;
+  if (g.gt == 0) needs[g.id] = b < a.batch ? warp_row_need(a, b) : 0;
   __syncthreads();
   if (b >= a.batch) return;
   int off = 0;
-  for (int v = 0; v < warp; v++) off += needs[v];
-  const int need = needs[warp];
-  const size_t wsb = warp_fin_bytes(a.ht_log2);
-  float* py = reinterpret_cast<float*>(dyn + static_cast<size_t>(W) * wsb);
+  for (int v = 0; v < g.id; v++) off += needs[v];
+  const int need = needs[g.id];
+  const size_t wsb = grp_fin_bytes(a.ht_log2);
+  float* py = reinterpret_cast<float*>(dyn + static_cast<size_t>(R) * wsb);
   int* pi = reinterpret_cast<int*>(py + pool_entries);
   const bool fits = need > 0 && off + need <= pool_entries;
-  const bool ok = warp_finish_row(a, b, dyn + static_cast<size_t>(warp) * wsb, fits ? py + off : nullptr,
-                                  fits ? pi + off : nullptr);
-  if (lane == 0) {
+  const bool ok = grp_finish_row<G>(g, a, b, dyn + static_cast<size_t>(g.id) * wsb, fits ? py + off : nullptr,
+                                    fits ? pi + off : nullptr);
+  if (g.gt == 0) {
     if (ok) {
       atomicAdd(&a.counters[0], 1ull);
       atomicAdd(&a.counters[6], 1ull);

@@ -181,7 +181,11 @@ int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_s
     e = s->cand.ensure(static_cast<size_t>(s->split_rows) * (static_cast<size_t>(tg::kCandMax) * 8 + 12) + 16);
   }
   if (e == cudaSuccess && s->split_rows) {
-    e = cudaFuncSetAttribute(tg::finish_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
+    e = cudaFuncSetAttribute(tg::finish_warp_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tg::finish_warp_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tg::finish_warp_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
   }
   if (e != cudaSuccess) {
     tg_sampler_destroy(s);
@@ -330,12 +334,21 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
       tg::sample_kernel<1, true><<<n, tg::kSampleNT, ring_smem, st>>>(c);
     if (mark) TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
     if (warp_fin) {  // a warp per row, then the rows it left on CTAs
-      // one CTA per SM: ceil(n / SMs) warps (rows) each, at most kWfMaxWarps
-      int wpc = (n + nsm - 1) / nsm;
-      wpc = wpc < 1 ? 1 : (wpc > tg::kWfMaxWarps ? tg::kWfMaxWarps : wpc);
-      const size_t wsb = static_cast<size_t>(wpc) * tg::warp_fin_bytes(a.ht_log2);
+      // one CTA per SM with ceil(n / SMs) rows; G warps per row, G the largest
+      // of 4, 2, 1 that keeps the CTA within 28 warps (register file at the
+      // kernel's register count) and 16 warps per row group in all
+      int rpc = (n + nsm - 1) / nsm;
+      rpc = rpc < 1 ? 1 : (rpc > tg::kWfMaxWarps ? tg::kWfMaxWarps : rpc);
+      const int G = rpc * 4 <= tg::kWfGroupWarps ? 4 : (rpc * 2 <= tg::kWfGroupWarps ? 2 : 1);
+      const size_t wsb = static_cast<size_t>(rpc) * tg::grp_fin_bytes(a.ht_log2);
       const int pool = static_cast<int>((static_cast<size_t>(tg::kWfSmem) - wsb) / 8);
-      tg::finish_warp_kernel<<<(n + wpc - 1) / wpc, wpc * 32, tg::kWfSmem, st>>>(c, pool);
+      const int grid = (n + rpc - 1) / rpc;
+      if (G == 4)
+        tg::finish_warp_kernel<4><<<grid, rpc * 128, tg::kWfSmem, st>>>(c, pool);
+      else if (G == 2)
+        tg::finish_warp_kernel<2><<<grid, rpc * 64, tg::kWfSmem, st>>>(c, pool);
+      else
+        tg::finish_warp_kernel<1><<<grid, rpc * 32, tg::kWfSmem, st>>>(c, pool);
       const int g = n < nsm * tg::kMinCtasPerSm ? n : nsm * tg::kMinCtasPerSm;
       if (dtype == TG_DTYPE_F32)
         tg::sample_list_kernel<0><<<g, tg::kSampleNT, smem, st>>>(c);
