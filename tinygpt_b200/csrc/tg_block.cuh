@@ -15,6 +15,18 @@ __device__ __forceinline__ unsigned long long radix_mass_of(const unsigned int (
          (static_cast<unsigned long long>(l[2][bin]) << 22) + (static_cast<unsigned long long>(l[3][bin]) << 33);
 }
 
+// Barrier of the NT threads of a CTA-wide stage: __syncthreads when BAR is 0,
+// else the named barrier BAR over NT threads (a warp-specialized CTA whose
+// other warps run other work).
+template <int NT, int BAR>
+__device__ __forceinline__ void bsync() {
+  if constexpr (BAR == 0) {
+    __syncthreads();
+  } else {
+    asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+  }
+}
+
 struct __align__(16) BlockScratch {
   // Mass histograms are kept as 32-bit limbs of the 64-bit sums: shared-memory
   // 32-bit atomic adds are native, 64-bit ones are compare-and-swap loops that
@@ -53,32 +65,32 @@ struct ReduceScratch {
   float red_f2[32];
 };
 
-template <int NT, class S>
+template <int NT, class S, int BAR = 0>
 __device__ __forceinline__ float block_max(float v, S& sm) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
   if ((threadIdx.x & 31) == 0) sm.red_f[threadIdx.x >> 5] = v;
-  __syncthreads();
+  bsync<NT, BAR>();
   float r = sm.red_f[0];
 #pragma unroll
   for (int i = 1; i < NT / 32; i++) r = fmaxf(r, sm.red_f[i]);
-  __syncthreads();
+  bsync<NT, BAR>();
   return r;
 }
 
 // Two maxima with one pair of barriers.
-template <int NT, class S>
+template <int NT, class S, int BAR = 0>
 __device__ __forceinline__ void block_max2(float& a, float& b, S& sm) {
   for (int o = 16; o > 0; o >>= 1) {
     a = fmaxf(a, __shfl_xor_sync(kFull, a, o));
     b = fmaxf(b, __shfl_xor_sync(kFull, b, o));
   }
   if ((threadIdx.x & 31) == 0) { sm.red_f[threadIdx.x >> 5] = a; sm.red_f2[threadIdx.x >> 5] = b; }
-  __syncthreads();
+  bsync<NT, BAR>();
   a = sm.red_f[0];
   b = sm.red_f2[0];
 #pragma unroll
   for (int i = 1; i < NT / 32; i++) { a = fmaxf(a, sm.red_f[i]); b = fmaxf(b, sm.red_f2[i]); }
-  __syncthreads();
+  bsync<NT, BAR>();
 }
 
 template <int NT, class S>
@@ -130,7 +142,7 @@ __device__ __forceinline__ void block_argmax(float& y, int& id, S& sm) {
 }
 
 // Exclusive prefix sum of one u64 per thread in thread order; also the total.
-template <int NT, class S>
+template <int NT, class S, int BAR = 0>
 __device__ __forceinline__ unsigned long long block_excl_scan(unsigned long long v,
                                                               unsigned long long& total,
                                                               S& sm) {
@@ -141,7 +153,7 @@ __device__ __forceinline__ unsigned long long block_excl_scan(unsigned long long
     if (lane >= o) incl += n;
   }
   if (lane == 31) sm.red_u64[w] = incl;
-  __syncthreads();
+  bsync<NT, BAR>();
   unsigned long long before = 0;
   total = 0;
 #pragma unroll
@@ -150,7 +162,7 @@ __device__ __forceinline__ unsigned long long block_excl_scan(unsigned long long
     if (i < w) before += s;
     total += s;
   }
-  __syncthreads();
+  bsync<NT, BAR>();
   return before + incl - v;
 }
 
@@ -224,11 +236,11 @@ __device__ __forceinline__ void hist_put(BlockScratch& sm, int bin, unsigned lon
   }
 }
 
-template <int NT, int NB, bool kMass, class Reached>
+template <int NT, int NB, bool kMass, class Reached, int BAR = 0>
 __device__ HistSel hist_scan(Reached reached, BlockScratch& sm) {
   constexpr int P = NB / NT;
   const int t = threadIdx.x;
-  __syncthreads();
+  bsync<NT, BAR>();
   unsigned long long v[P];
   unsigned long long loc = 0;
 #pragma unroll
@@ -240,7 +252,7 @@ __device__ HistSel hist_scan(Reached reached, BlockScratch& sm) {
     loc += v[j];
   }
   unsigned long long tot;
-  const unsigned long long bef = block_excl_scan<NT>(loc, tot, sm);
+  const unsigned long long bef = block_excl_scan<NT, BlockScratch, BAR>(loc, tot, sm);
   if (!reached(bef) && reached(bef + loc)) {
     unsigned long long c = bef;
 #pragma unroll
@@ -254,22 +266,22 @@ __device__ HistSel hist_scan(Reached reached, BlockScratch& sm) {
       c += v[j];
     }
   }
-  __syncthreads();
+  bsync<NT, BAR>();
   HistSel r{static_cast<int>(sm.sel_bin), sm.sel_before, sm.sel_mass};  // bin -1: not reached
-  __syncthreads();
+  bsync<NT, BAR>();
   return r;
 }
 
-template <int NT, int NB, bool kMass, class Src, class BinW, class Reached>
+template <int NT, int NB, bool kMass, class Src, class BinW, class Reached, int BAR = 0>
 __device__ HistSel hist_round(const Src& src, BinW binw, Reached reached, BlockScratch& sm) {
   hist_zero<NT, NB, kMass>(sm);
-  __syncthreads();
+  bsync<NT, BAR>();
   src.for_each([&](int i, float y) {
     int bin;
     unsigned long long w;
     if (binw(i, y, bin, w)) hist_put<kMass>(sm, bin, w);
   });
-  return hist_scan<NT, NB, kMass>(reached, sm);
+  return hist_scan<NT, NB, kMass, Reached, BAR>(reached, sm);
 }
 
 // Collect the elements for which member(i, y, key, w, id) holds into the small

@@ -85,6 +85,11 @@ __device__ __forceinline__ uint64_t draw_point(float u, uint64_t total) {
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
+// Shared-memory address of a generic pointer into shared memory.
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
 // 128-bit streaming load that bypasses L1 (data is read once per row).
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
   uint4 v;

@@ -40,7 +40,7 @@ constexpr int kWfMaxHist = 1024;     // longest history served (hash of 2048 slo
 constexpr int kWfBloomWords = 256;   // 8192-bit Bloom filter of the history ids
 
 // A group of G warps that finishes one row.  G == 1 synchronizes with
-// __syncwarp; larger groups with the named barrier id + 1 (ids 1..15; id 0 is
+// __syncwarp; larger groups with their own named barrier `bar` (1..15; 0 is
 // __syncthreads').
 template <int G>
 struct Grp {
@@ -49,11 +49,12 @@ struct Grp {
   int gt;    // thread index in the group
   int gw;    // warp index in the group
   int lane;
+  int bar;   // named barrier of the group (G > 1)
   __device__ __forceinline__ void sync() const {
     if constexpr (G == 1) {
       __syncwarp();
     } else {
-      asm volatile("bar.sync %0, %1;" ::"r"(id + 1), "n"(NT) : "memory");
+      asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(NT) : "memory");
     }
   }
 };
@@ -322,24 +323,42 @@ __device__ __forceinline__ int warp_row_need(const SampleArgs& a, int b) {
   return (greedy || topk) ? n : 0;
 }
 
-// A group of G warps finishes row b over its list staged in ly / lid (this
-// row's share of the pool, null when the pool had no room).  Returns false
-// when the row is left for the fallback kernel; the global list is only read.
+// Whether a finisher group takes row b, whose list holds n elements >= theta
+// (n > kCandMax: the list overflowed).  Decided before the list is touched.
+__device__ __forceinline__ bool grp_can_take(const SampleArgs& a, int b, int n, float theta) {
+  if (n <= 0 || n > kCandMax || !(theta > neg_inf())) return false;
+  const tg_row_params p = a.params[b];
+  const bool greedy = !(p.temperature > 0.0f);
+  const bool topk = p.top_k > 0 && p.top_k < a.vocab;
+  if (!greedy && !topk) return false;
+  int hlen = 0;
+  if (a.history_len && a.history && a.hist_cap > 0) {
+    hlen = a.history_len[b];
+    hlen = hlen < 0 ? 0 : (hlen > a.hist_cap ? a.hist_cap : hlen);
+  }
+  const bool pf_on = p.presence_penalty != 0.0f || p.frequency_penalty != 0.0f;
+  const bool need_hist = hlen > 0 && (p.repetition_penalty > 1.0f || pf_on);
+  if (need_hist && pf_on && (p.presence_penalty < 0.0f || p.frequency_penalty < 0.0f)) return false;
+  if (need_hist && hlen > kWfMaxHist) return false;
+  return true;
+}
+
+// A group of G warps finishes row b (grp_can_take holds) over its list of n
+// elements >= theta in ly / lid: staged there first from the global list when
+// kFromGlobal, else already there (the fused kernel's slot).  The list is
+// modified in place (penalties, compaction); the global list is only read.
+// Returns false when the row is left for a fallback.
 // Element i of the list belongs to warp (i / 32) % G; after the compaction each
 // warp keeps its survivors in its own slots, in place (slot(j) below), so no
 // cross-warp prefix is needed.
-template <int G>
-__device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsigned char* scratch, float* ly,
-                               int* lid) {
+template <int G, bool kFromGlobal>
+__device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, int n, float theta,
+                               unsigned char* scratch, float* ly, int* lid) {
   constexpr int NT = 32 * G;
   const int lane = g.lane, gt = g.gt;
-  if (ly == nullptr) return false;
-  const int n = a.cand_gn[b];
   const tg_row_params p = a.params[b];
   const int V = a.vocab;
   const bool greedy = !(p.temperature > 0.0f);
-  const float theta = a.cand_gth[b];
-  if (!(theta > neg_inf())) return false;
   int hlen = 0;
   if (a.history_len && a.history && a.hist_cap > 0) {
     hlen = a.history_len[b];
@@ -348,8 +367,6 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
   const bool rep_on = p.repetition_penalty > 1.0f;
   const bool pf_on = p.presence_penalty != 0.0f || p.frequency_penalty != 0.0f;
   const bool need_hist = hlen > 0 && (rep_on || pf_on);
-  if (need_hist && pf_on && (p.presence_penalty < 0.0f || p.frequency_penalty < 0.0f)) return false;
-  if (need_hist && hlen > kWfMaxHist) return false;
 
   uint32_t* bloom = reinterpret_cast<uint32_t*>(scratch);
   uint32_t* hash = bloom + kWfBloomWords;
@@ -361,7 +378,7 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
 
   // stage the list: 16 loads in flight per thread, straight to shared memory
   constexpr int LU = 16;
-  for (int base = gt; base < n; base += NT * LU) {
+  for (int base = gt; kFromGlobal && base < n; base += NT * LU) {
     float yv[LU];
     int iv[LU];
 #pragma unroll
@@ -411,6 +428,7 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
   }
   g.sync();
   wc.mark(0);  // 16: staging and hash build
+  if (a.debug_stop == 1) return false;
   auto count_of = [&](int id) {
     const uint32_t bit = wf_bloom_bit(id);
     if (!((bloom[bit >> 5] >> (bit & 31)) & 1u)) return 0;
@@ -476,6 +494,7 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
     g.sync();
   }
   wc.mark(1);  // 17: penalty pass
+  if (a.debug_stop == 2) return false;
 
   const unsigned int need = greedy ? 1u : static_cast<unsigned int>(p.top_k);
   if (cnt < need) return false;
@@ -505,6 +524,7 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
       [&](unsigned long long c) { return c >= k; }, ws, kk, kb, kw);
   if (!okk) return false;
   wc.mark(2);  // 18: k-th value
+  if (a.debug_stop == 3) return false;
   const float kth = key2f(~kk);
   const float sk = __fdiv_rn(kth, T);
   const float below = key2f(fkey(theta) - 1u);  // every absent value is <= below
@@ -555,6 +575,7 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
   __syncwarp();
   Q = grp_sum(g, ws, Q);  // its barriers also publish the top-p histogram
   wc.mark(3);  // 19: compaction and Q
+  if (a.debug_stop == 4) return false;
 
   auto mass = [&](float sv) { return qmass_le0(__fsub_rn(sv, smax)); };
   // (d) top-p: the last element (cut_key, cut_id) of the shortest prefix in
@@ -600,6 +621,7 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
     }
   }
   wc.mark(4);  // 20: top-p
+  if (a.debug_stop == 5) return false;
   const bool minpon = p.min_p > 0.0f;
   const double minq = __dmul_rn(static_cast<double>(fminf(p.min_p, 1.0f)), static_cast<double>(kMassScale));
   auto kept_mass = [&](float sv, int id) {
@@ -627,6 +649,7 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
   S = grp_sum(g, ws, S);
   if (S == 0) return false;
   wc.mark(5);  // 21: kept mass S
+  if (a.debug_stop == 6) return false;
 
   // (e) draw: the first id in index order whose running mass exceeds r
   const unsigned long long r = draw_point(a.uniforms ? a.uniforms[b] : 0.0f, S);
@@ -645,6 +668,7 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, unsi
       static_cast<uint32_t>(V - 1), true, [&](unsigned long long c) { return c > r; }, ws, pk, pb, pw);
   if (!okd) return false;
   wc.mark(6);  // 22: draw
+  if (a.debug_stop == 7) return false;
   if (gt == 0) {
     a.out_ids[b] = static_cast<int>(pk);
     if (a.out_probs) a.out_probs[b] = __double2float_rn(__ddiv_rn(__ull2double_rn(pw), __ull2double_rn(S)));
@@ -662,7 +686,8 @@ __global__ void __launch_bounds__(kWfMaxNT, 1) finish_warp_kernel(SampleArgs a, 
   __shared__ int needs[kWfMaxWarps];
   const int R = blockDim.x / (32 * G);  // rows of this CTA
   const Grp<G> g{static_cast<int>(threadIdx.x) / (32 * G), static_cast<int>(threadIdx.x) % (32 * G),
-                 (static_cast<int>(threadIdx.x) % (32 * G)) >> 5, static_cast<int>(threadIdx.x) & 31};
+                 (static_cast<int>(threadIdx.x) % (32 * G)) >> 5, static_cast<int>(threadIdx.x) & 31,
+                 static_cast<int>(threadIdx.x) / (32 * G) + 1};
   const int b = blockIdx.x * R + g.id;
   if (g.gt == 0) needs[g.id] = b < a.batch ? warp_row_need(a, b) : 0;
   __syncthreads();
@@ -674,8 +699,10 @@ __global__ void __launch_bounds__(kWfMaxNT, 1) finish_warp_kernel(SampleArgs a, 
   float* py = reinterpret_cast<float*>(dyn + static_cast<size_t>(R) * wsb);
   int* pi = reinterpret_cast<int*>(py + pool_entries);
   const bool fits = need > 0 && off + need <= pool_entries;
-  const bool ok = grp_finish_row<G>(g, a, b, dyn + static_cast<size_t>(g.id) * wsb, fits ? py + off : nullptr,
-                                    fits ? pi + off : nullptr);
+  const int n = a.cand_gn[b];
+  const float theta = a.cand_gth[b];
+  const bool ok = fits && grp_can_take(a, b, n, theta) &&
+                  grp_finish_row<G, true>(g, a, b, n, theta, dyn + static_cast<size_t>(g.id) * wsb, py + off, pi + off);
   if (g.gt == 0) {
     if (ok) {
       atomicAdd(&a.counters[0], 1ull);

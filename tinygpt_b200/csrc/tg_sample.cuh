@@ -119,6 +119,7 @@ struct SampleArgs {
   // warp finisher: rows it left for sample_list_kernel, and their count
   int32_t* fb_rows;
   int32_t* fb_count;
+  int32_t debug_stop;  // diagnostics: the warp finisher leaves rows after this stage (0: off)
 };
 
 // History hash in shared memory: key = token id (-1 empty); val = count, then
@@ -977,7 +978,7 @@ __device__ bool finish_cands(float* cy, int* cid, float* ce, int n, float theta,
 // bins of equal width between the largest and the smallest finite maximum,
 // then the smallest maximum inside the bin that holds the rk-th largest (a
 // lower bound of the rk-th largest; -inf when rk exceeds the sample).
-template <int N, int NT = kSampleNT>
+template <int N, int NT = kSampleNT, int BAR = 0>
 __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm) {
   float mx = neg_inf(), nmn = neg_inf();
 #pragma unroll
@@ -985,7 +986,7 @@ __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm
     mx = fmaxf(mx, vm[i]);
     if (vm[i] > neg_inf()) nmn = fmaxf(nmn, -vm[i]);
   }
-  block_max2<NT>(mx, nmn, sm);
+  block_max2<NT, BlockScratch, BAR>(mx, nmn, sm);
   const float mn = -nmn;
   if (mx == neg_inf()) return neg_inf();
   const float width = __fsub_rn(mx, mn);
@@ -995,15 +996,15 @@ __device__ float sample_theta(const float* vm, unsigned int rk, BlockScratch& sm
     const int bn = static_cast<int>(__fmul_rn(__fsub_rn(mx, v), scale));
     return bn > 2046 ? 2046 : bn;
   };
-  const HistSel hs = hist_round<NT, 2048, false>(
-      RegSrc<N>{vm}, [&](int, float v, int& bin, unsigned long long& w) { bin = binf(v); w = 1; return true; },
-      [&](unsigned long long c) { return c >= rk; }, sm);
+  auto bw = [&](int, float v, int& bin, unsigned long long& w) { bin = binf(v); w = 1; return true; };
+  auto reached = [&](unsigned long long c) { return c >= rk; };
+  const HistSel hs = hist_round<NT, 2048, false, RegSrc<N>, decltype(bw), decltype(reached), BAR>(RegSrc<N>{vm}, bw, reached, sm);
   if (hs.bin < 0 || hs.bin == 2047) return neg_inf();
   float nlo = neg_inf();
 #pragma unroll
   for (int i = 0; i < N; i++)
     if (binf(vm[i]) == hs.bin) nlo = fmaxf(nlo, -vm[i]);
-  return -block_max<NT>(nlo, sm);
+  return -block_max<NT, BlockScratch, BAR>(nlo, sm);
 }
 
 // Vocab-sharded mode, local half: the record of one row -- every local value

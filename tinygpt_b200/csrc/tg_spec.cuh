@@ -80,10 +80,6 @@ __device__ __forceinline__ const uint32_t* spec_mask(const SpecArgs& a, int b, i
 
 __device__ __forceinline__ float spec_T(float t0) { return fmaxf(t0, 1e-5f); }
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
 // Bounded wait on phase 0 of an mbarrier; false when the limit ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar) {
   for (unsigned it = 0; it < kWaitLimit; it++) {

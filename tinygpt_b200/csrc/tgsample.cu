@@ -16,6 +16,7 @@
 #include "../../include/tgsample.h"
 #include "tg_sample.cuh"
 #include "tg_finish_warp.cuh"
+#include "tg_fused.cuh"
 #include "tg_spec.cuh"
 
 namespace {
@@ -131,7 +132,15 @@ bool getenv_off(const char* name) {
 // kCandMax * 8 + 8 bytes per row).
 constexpr int kSplitRows = 4096;
 // The two-kernel mode pays for itself from this many rows on.
-constexpr int kSplitMinBatch = 1024;
+constexpr int kSplitMinBatchDefault = 1024;
+// TG_SPLIT_MIN_BATCH overrides it (diagnostics: the two-kernel mode on small batches).
+int split_min_batch() {
+  static const int v = [] {
+    const char* e = getenv("TG_SPLIT_MIN_BATCH");
+    return e ? atoi(e) : kSplitMinBatchDefault;
+  }();
+  return v;
+}
 }  // namespace
 
 extern "C" {
@@ -172,9 +181,9 @@ int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_s
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tg::sample_kernel<1, false, tg::kWideNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   // the two-kernel mode serves rows longer than a candidate list, in batches of
-  // kSplitMinBatch rows or more (TG_SAMPLE_SPLIT=0 turns it off)
+  // split_min_batch() rows or more (TG_SAMPLE_SPLIT=0 turns it off)
   const char* split_env = getenv("TG_SAMPLE_SPLIT");
-  if (e == cudaSuccess && vocab > tg::kCandMax && max_batch >= kSplitMinBatch &&
+  if (e == cudaSuccess && vocab > tg::kCandMax && max_batch >= split_min_batch() &&
       !(split_env && split_env[0] == '0')) {
     s->split_rows = max_batch < kSplitRows ? max_batch : kSplitRows;
     // per row: the list (value, id), its length and theta, a fallback-list slot; one count
@@ -186,6 +195,10 @@ int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_s
       e = cudaFuncSetAttribute(tg::finish_warp_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tg::finish_warp_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tg::sample_fused_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kFuSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tg::sample_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kFuSmem);
   }
   if (e != cudaSuccess) {
     tg_sampler_destroy(s);
@@ -259,6 +272,10 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
   a.out_ids = out_ids;
   a.out_probs = out_probs;
   a.status = s->d_status;
+  {
+    const char* ds = getenv("TG_WF_STOP");
+    a.debug_stop = ds ? atoi(ds) : 0;
+  }
   a.counters = s->d_counters;
   const size_t smem = static_cast<size_t>(tg::kCandMax) * 12 + (a.ht_log2 ? (size_t(8) << a.ht_log2) : 0);
   DeviceGuard g(s->device);
@@ -280,7 +297,7 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
     }
     return TG_OK;
   }
-  if (s->split_rows == 0 || batch < kSplitMinBatch) {
+  if (s->split_rows == 0 || batch < split_min_batch()) {
     if (dtype == TG_DTYPE_F32)
       tg::sample_kernel<0><<<batch, tg::kSampleNT, smem, st>>>(a);
     else
@@ -312,6 +329,23 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
   }
   int nsm = 148;
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, s->device);
+  // the fused kernel (streaming and finishing in one persistent launch): the
+  // most ring stages (3..6) that fit next to 4 list slots and 3 finisher groups
+  tg::FusedCfg fcfg{};
+  // (opt-in with TG_FUSED=1: measured slower than the two launches so far --
+  // 458 vs 194 us per config-4 call -- its filter and finisher warps are too
+  // few per SM to hide their latency)
+  const char* fenv = getenv("TG_FUSED");
+  bool fused = warp_fin && fenv && fenv[0] == '1';
+  if (fused) {
+    int st = 6;
+    while (st >= 3 && tg::fused_smem(st, 4, 3, a.ht_log2, nullptr) > static_cast<size_t>(tg::kFuSmem)) st--;
+    fused = st >= 3;
+    if (fused) tg::fused_smem(st, 4, 3, a.ht_log2, &fcfg);
+    const char* dbg = getenv("TG_FUSED_DEBUG");
+    fcfg.debug = dbg ? atoi(dbg) : 0;
+  }
+  const size_t fsmem = fused ? tg::fused_smem(fcfg.stages, fcfg.slots, fcfg.groups, a.ht_log2, nullptr) : 0;
   const size_t ring_smem = static_cast<size_t>(tg::kSampleNT / 32) * tg::kRing * 20;
   const int64_t es = dtype == TG_DTYPE_F32 ? 4 : 2;
   for (int32_t r0 = 0; r0 < batch; r0 += R) {
@@ -328,6 +362,23 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
     if (c.out_probs) c.out_probs = out_probs + r0;
     if (c.shard_out) c.shard_out = shard_out + r0;
     const bool mark = s->profile && r0 == 0 && n == batch;  // single launch pair: time each kernel
+    if (fused) {  // one persistent kernel per SM, then the rows it left on CTAs
+      TG_CUDA(cudaMemsetAsync(c.fb_count, 0, sizeof(int32_t), st));
+      const int grid = n < nsm ? n : nsm;
+      const int threads = tg::kFuFinTid0 + fcfg.groups * 32 * tg::kFuG;
+      if (dtype == TG_DTYPE_F32)
+        tg::sample_fused_kernel<0><<<grid, threads, fsmem, st>>>(c, fcfg);
+      else
+        tg::sample_fused_kernel<1><<<grid, threads, fsmem, st>>>(c, fcfg);
+      if (mark) TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
+      const int g = n < nsm * tg::kMinCtasPerSm ? n : nsm * tg::kMinCtasPerSm;
+      if (dtype == TG_DTYPE_F32)
+        tg::sample_list_kernel<0><<<g, tg::kSampleNT, smem, st>>>(c);
+      else
+        tg::sample_list_kernel<1><<<g, tg::kSampleNT, smem, st>>>(c);
+      TG_CUDA(cudaGetLastError());
+      continue;
+    }
     if (dtype == TG_DTYPE_F32)
       tg::sample_kernel<0, true><<<n, tg::kSampleNT, ring_smem, st>>>(c);
     else
