@@ -20,7 +20,13 @@
  * Memory: all array arguments of tg_sample / tg_spec_verify are DEVICE pointers
  * on the sampler's device, owned by the caller.  The *_host variants take host
  * pointers and stage through buffers the handle owns.  Threading: one handle
- * per device; a handle is not shared between threads without external locking.
+ * per device; a handle is not shared between threads without external locking,
+ * and serves one stream at a time: its candidate buffer, status word, counters
+ * and statistics are per handle, so calls on one handle from two streams that
+ * can overlap on the GPU race (use one handle per stream).
+ * Allocation: tg_sample allocates nothing (its buffers are made by
+ * tg_sampler_create); tg_spec_verify and tg_sample_sharded use buffers made by
+ * tg_sampler_reserve and return TG_ERR_UNSUPPORTED for calls beyond them.
  *
  * Semantics (bit-exact definition, restated by the CPU oracle):
  *   y[v]   = logits[v] (bf16 widened exactly to fp32)
@@ -54,6 +60,7 @@ extern "C" {
 #define TG_ERR_UNSUPPORTED   -3  /* size beyond a compiled limit                  */
 #define TG_ERR_NO_DEVICE     -4  /* device index not present                      */
 #define TG_ERR_DEVICE_STATUS -5  /* a kernel reported a data error (see below)    */
+#define TG_ERR_COLLECTIVE    -6  /* a collective missed its deadline; the communicator was aborted */
 
 /* ---- dtypes of the logits --------------------------------------------------- */
 #define TG_DTYPE_F32   0
@@ -147,6 +154,10 @@ int32_t tg_sample_host(tg_sampler* s, const void* logits, int32_t dtype,
  *                 (SpeculativeDecode.swift:41-98), > 0 stochastic with
  *                 T = max(temperature, 1e-5) (SpeculativeDecode.swift:121-210)
  *   u_accept      [batch, K] float uniforms for the accept tests
+ *   draft_logits and u_accept may both be NULL (greedy verification without a
+ *   draft distribution: Medusa / EAGLE heads, MedusaHeads.swift:186-265,
+ *   EagleDraft.swift:216-290); a stochastic row then ends without a token
+ *   (out_n = 0) and sets device status bit 4
  *   u_draw        [batch] float uniform for the residual / bonus draw
  *   out_ids       [batch, K+1] int32: accepted proposals then the final token;
  *                 entries past out_n are set to -1
@@ -154,7 +165,8 @@ int32_t tg_sample_host(tg_sampler* s, const void* logits, int32_t dtype,
  * Accept iff u <= min(1, pT(tok) / max(pD(tok), 1e-10)).  On the first reject
  * the final token is drawn from max(0, pT - pD) renormalised when its mass
  * exceeds 1e-10, else from pT; after K accepts it is the bonus drawn from pT at
- * position K.  Probabilities are q / sum(q) with q the exact masses above. */
+ * position K.  Probabilities are q / sum(q) with q the exact masses above.
+ * Needs statistics reserved by tg_sampler_reserve(s, >= K, ...). */
 int32_t tg_spec_verify(tg_sampler* s, const void* target_logits,
                        const void* draft_logits, int32_t dtype, int32_t batch,
                        int32_t K, const int32_t* draft_ids,
@@ -194,7 +206,9 @@ int32_t tg_spec_verify_masked(tg_sampler* s, const void* target_logits,
  * before any stream capture.  All calls on a device share the array, so calls
  * that overlap on the GPU (different streams without ordering) race.
  * Arguments and results are those of tg_spec_verify, on CUDA device `device`;
- * an out-of-range draft id counts as a rejection and is not reported. */
+ * data errors (bits 1, 3 and 4 of the device status word) are kept in a status
+ * word inside the same array, cleared at the start of every call and read by
+ * tg_spec_verify_static_status. */
 #define TG_STATIC_SPEC_MAX_ROWS 8192
 int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_logits,
                               const void* draft_logits, int32_t dtype, int32_t batch,
@@ -202,6 +216,21 @@ int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_
                               const float* temperature, const float* u_accept,
                               const float* u_draw, int32_t* out_ids, int32_t* out_n,
                               void* stream);
+
+/* Status bits of the last tg_spec_verify_static call on `device` (meaning as
+ * tg_sampler_device_status); synchronizes the device, clears the word,
+ * allocates nothing.  No counterpart in the reference. */
+int32_t tg_spec_verify_static_status(int32_t device, uint32_t* out_bits);
+
+/* Makes the buffers of the calls that need more than tg_sampler_create's:
+ * verification statistics for max_batch rows of up to max_K proposals
+ * (tg_spec_verify, tg_spec_verify_masked) and, when max_ranks > 0, the record
+ * storage of tg_sample_sharded for communicators of up to max_ranks ranks
+ * ((max_ranks + 1) x max_batch x 10,256 bytes).  Buffers only grow.  Call it
+ * before the hot loop (and before any stream capture); the hot calls then
+ * allocate nothing.  No counterpart in the reference (its C ABI has no
+ * device buffers, wasm/src/model.h:39-43). */
+int32_t tg_sampler_reserve(tg_sampler* s, int32_t max_K, int32_t max_ranks);
 
 /* ---- vocab-sharded mode (one process per GPU, each owning a vocab slice) ----
  * For vocabularies or batches where one GPU should not hold whole rows: rank r
@@ -251,8 +280,12 @@ int32_t tg_sample_shard_merge(tg_sampler* s, const tg_shard_record* records, int
  * `stream`; every rank gets the same ids.  Arguments otherwise as tg_sample,
  * for this rank's slice of every row.  NCCL is not linked: ncclAllGather is
  * looked up in the NCCL the process has loaded (TG_ERR_UNSUPPORTED if none).
- * Record storage ((nranks + 1) x batch x 10,256 bytes) is allocated on the
- * first call and grows with batch and nranks.  Limits as the two halves
+ * Record storage comes from tg_sampler_reserve(s, ..., >= nranks); nranks must
+ * equal the communicator's size (checked with ncclCommCount).  With a collective
+ * timeout set (tg_sampler_set_collective_timeout) the call waits on the host for
+ * the all-gather and, when it misses the deadline (a rank that left), aborts the
+ * communicator (ncclCommAbort) and returns TG_ERR_COLLECTIVE; with none (the
+ * default) it only enqueues.  Limits as the two halves
  * (tg_sample_shard_local / tg_sample_shard_merge).  No counterpart in the
  * reference, which samples every row on one device. */
 int32_t tg_sample_sharded(tg_sampler* s, void* nccl_comm, int32_t nranks, int32_t vocab_offset,
@@ -262,13 +295,18 @@ int32_t tg_sample_sharded(tg_sampler* s, void* nccl_comm, int32_t nranks, int32_
                           const uint32_t* mask_table, int32_t num_states, const int32_t* state_id,
                           const float* uniforms, int32_t* out_ids, float* out_probs, void* stream);
 
+/* Deadline of tg_sample_sharded's all-gather in milliseconds (0: no host wait,
+ * the default).  The reference has no collective (single device). */
+int32_t tg_sampler_set_collective_timeout(tg_sampler* s, int32_t timeout_ms);
+
 /* Device error word of the last completed call on this handle (synchronizes
  * the handle's device).  Bit 0: a state_id outside [0, num_states);
  * bit 1: a draft id outside [0, vocab); bit 2: a row the vocab-sharded mode
  * could not resolve (unsupported parameters, more than TG_SHARD_CAP local
  * survivors, or a top-k threshold tie between shards); bit 3: a bounded wait
  * for a bulk copy into shared memory gave up (the affected statistics are
- * unreliable).  Cleared by this call. */
+ * unreliable); bit 4: a stochastic row in a verification called without
+ * draft logits (it ends without a token).  Cleared by this call. */
 int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits);
 
 /* Per-handle path counters of tg_sample (diagnostics, the device-side analogue

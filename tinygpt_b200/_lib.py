@@ -19,6 +19,7 @@ TG_ERR_CUDA = -2
 TG_ERR_UNSUPPORTED = -3
 TG_ERR_NO_DEVICE = -4
 TG_ERR_DEVICE_STATUS = -5
+TG_ERR_COLLECTIVE = -6
 TG_DTYPE_F32 = 0
 TG_DTYPE_BF16 = 1
 TG_MAX_VOCAB = 1 << 20
@@ -38,6 +39,7 @@ ROW_PARAMS_DTYPE = np.dtype([
 EXPORTED = ["tg_abi_version", "tg_last_error_string", "tg_sampler_create", "tg_sampler_destroy",
             "tg_sample", "tg_sample_host", "tg_spec_verify", "tg_sampler_device_status", "tg_sampler_path_counters",
             "tg_spec_verify_static", "tg_sample_shard_local", "tg_sample_shard_merge", "tg_sampler_profile", "tg_spec_verify_masked", "tg_sample_sharded",
+            "tg_sampler_reserve", "tg_sampler_set_collective_timeout", "tg_spec_verify_static_status",
             "tg_grammar_last_error", "tg_grammar_create", "tg_grammar_destroy",
             "tg_grammar_state_create", "tg_grammar_state_destroy", "tg_grammar_accept_bytes",
             "tg_grammar_kind", "tg_grammar_state_clone",
@@ -94,6 +96,12 @@ def load(path: str = LIB_PATH):
     L.tg_sample_sharded.argtypes = [vp, vp, i32, i32, i32, vp, i32, i64, i32, vp, vp, vp, i32, vp, i32, vp,
                                     vp, vp, vp, vp]
     L.tg_sample_sharded.restype = i32
+    L.tg_sampler_reserve.argtypes = [vp, i32, i32]
+    L.tg_sampler_reserve.restype = i32
+    L.tg_sampler_set_collective_timeout.argtypes = [vp, i32]
+    L.tg_sampler_set_collective_timeout.restype = i32
+    L.tg_spec_verify_static_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32)]
+    L.tg_spec_verify_static_status.restype = i32
     L.tg_sampler_profile.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(i32)]
     L.tg_sampler_profile.restype = i32
     L.tg_grammar_last_error.argtypes = []

@@ -159,7 +159,9 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const int V = a.vocab;
   const float t0 = a.temperature[b];
   const bool greedy = !(t0 > 0.0f);
-  if (pos > a.K && greedy) return;  // the whole cluster: the draft row is not needed
+  // the whole cluster: the draft row is not needed (greedy row, or a call
+  // without draft logits)
+  if (pos > a.K && (greedy || !a.draft)) return;
   const char* row;
   if (pos <= a.K) {
     row = reinterpret_cast<const char*>(a.target) + (static_cast<int64_t>(b) * (a.K + 1) + pos) * V * E::kSize;
@@ -202,7 +204,9 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   if (msk && id == 0x7fffffff) id = -1;  // nothing allowed above -inf
   if (greedy) {
     if (rank == 0 && t == 0) a.stats[r] = SpecStat{y, id, 0ull};
+    if (!ok && t == 0) atomicOr(a.status, 8u);
     cluster.sync();  // peers still read this CTA's maximum
+    if (!ok && bulk) mbar_wait(&bar);  // the copy that gave up must not land after the CTA exits
     return;
   }
   const float T = spec_T(t0);
@@ -248,6 +252,11 @@ __device__ __forceinline__ void spec_accept_step(const SpecArgs& a, int b, int i
     const int am = st[i].argmax;
     out[n++] = am;
     if (am != tok) fin = -2;
+    return;
+  }
+  if (!a.draft) {  // draft-free call: a stochastic row ends without a token
+    atomicOr(a.status, 16u);
+    fin = -2;
     return;
   }
   bool accept = false;
@@ -308,7 +317,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const SpecStat* st = a.stats + static_cast<int64_t>(b) * P;
   int32_t* out = a.out_ids + static_cast<int64_t>(b) * (K + 1);
   const char* tgt = reinterpret_cast<const char*>(a.target) + static_cast<int64_t>(b) * (K + 1) * V * E::kSize;
-  const char* drf = greedy ? nullptr : reinterpret_cast<const char*>(a.draft) + static_cast<int64_t>(b) * K * V * E::kSize;
+  const char* drf = (greedy || !a.draft) ? nullptr : reinterpret_cast<const char*>(a.draft) + static_cast<int64_t>(b) * K * V * E::kSize;
 
   if (rank == 0 && t == 0) {
     int n = 0, fin = -1;

@@ -12,6 +12,8 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <chrono>
+#include <thread>
 
 #include "../../include/tgsample.h"
 #include "tg_sample.cuh"
@@ -118,6 +120,8 @@ struct tg_sampler {
   bool profile = false;
   cudaEvent_t prof_ev[3] = {nullptr, nullptr, nullptr};
   int prof_kind = 0;  // 0: no call recorded, 1: one kernel, 2: two kernels
+  int coll_timeout_ms = 0;        // tg_sample_sharded: 0 = no host wait
+  cudaEvent_t coll_ev = nullptr;
   std::mutex mu;
 };
 
@@ -219,6 +223,7 @@ int32_t tg_sampler_destroy(tg_sampler* s) {
     s->shard_recs.release();
     for (cudaEvent_t ev : s->prof_ev)
       if (ev) cudaEventDestroy(ev);
+    if (s->coll_ev) cudaEventDestroy(s->coll_ev);
     for (DevBuf* b : {&s->h_logits, &s->h_params, &s->h_hist, &s->h_hlen, &s->h_mask, &s->h_state,
                       &s->h_unif, &s->h_out, &s->h_prob})
       b->release();
@@ -488,6 +493,44 @@ static tg_nccl_allgather_fn nccl_allgather() {
   return fn;
 }
 
+typedef int (*tg_nccl_count_fn)(void*, int*);
+typedef int (*tg_nccl_abort_fn)(void*);
+
+// A symbol of the NCCL the process has loaded (global scope first, then an
+// NCCL loaded with local scope, found by its soname), or nullptr.
+static void* nccl_symbol(const char* name) {
+  void* sym = dlsym(RTLD_DEFAULT, name);
+  for (const char* lib : {"libnccl.so.2", "libnccl.so"}) {
+    if (sym) break;
+    void* h = dlopen(lib, RTLD_LAZY | RTLD_NOLOAD);
+    if (h) sym = dlsym(h, name);
+  }
+  return sym;
+}
+static tg_nccl_count_fn nccl_comm_count() { return reinterpret_cast<tg_nccl_count_fn>(nccl_symbol("ncclCommCount")); }
+static tg_nccl_abort_fn nccl_comm_abort() { return reinterpret_cast<tg_nccl_abort_fn>(nccl_symbol("ncclCommAbort")); }
+
+// Waits for the work queued on `stream` (the all-gather) for at most the
+// handle's collective timeout.  On expiry the communicator is aborted (its
+// pending collectives then end with an error) and TG_ERR_COLLECTIVE returned.
+static int32_t wait_collective(tg_sampler* s, void* comm, cudaStream_t stream) {
+  DeviceGuard g(s->device);
+  if (!s->coll_ev) TG_CUDA(cudaEventCreateWithFlags(&s->coll_ev, cudaEventDisableTiming));
+  TG_CUDA(cudaEventRecord(s->coll_ev, stream));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(s->coll_ev);
+    if (q == cudaSuccess) return TG_OK;
+    if (q != cudaErrorNotReady) return cuda_fail(q, "cudaEventQuery (collective)");
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+    if (ms >= s->coll_timeout_ms) break;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  const tg_nccl_abort_fn abort_fn = nccl_comm_abort();
+  if (abort_fn) abort_fn(comm);
+  return fail(TG_ERR_COLLECTIVE, "the all-gather did not complete within the collective timeout; the communicator was aborted");
+}
+
 int32_t tg_sample_sharded(tg_sampler* s, void* nccl_comm, int32_t nranks, int32_t vocab_offset,
                           int32_t full_vocab, const void* logits, int32_t dtype, int64_t row_stride,
                           int32_t batch, const tg_row_params* params, const int32_t* history,
@@ -497,16 +540,26 @@ int32_t tg_sample_sharded(tg_sampler* s, void* nccl_comm, int32_t nranks, int32_
   if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
   if (!nccl_comm || nranks <= 0) return fail(TG_ERR_INVALID_ARG, "nccl_comm and nranks > 0 are required");
   if (batch < 0 || batch > s->max_batch) return fail(TG_ERR_INVALID_ARG, "batch outside [0, max_batch]");
+  if (vocab_offset < 0 || full_vocab > TG_MAX_VOCAB || static_cast<int64_t>(vocab_offset) + s->vocab > full_vocab)
+    return fail(TG_ERR_INVALID_ARG, "shard [vocab_offset, vocab_offset + vocab) outside [0, full_vocab <= TG_MAX_VOCAB)");
   if (batch == 0) return TG_OK;
   if (!out_ids) return fail(TG_ERR_INVALID_ARG, "out_ids is required");
   const tg_nccl_allgather_fn allgather = nccl_allgather();
   if (!allgather) return fail(TG_ERR_UNSUPPORTED, "no NCCL library is loaded in this process (ncclAllGather not found)");
-  const size_t rec = sizeof(tg_shard_record) * static_cast<size_t>(batch);
-  {
-    std::lock_guard<std::mutex> lk(s->mu);
-    DeviceGuard g(s->device);
-    TG_CUDA(s->shard_recs.ensure(rec * (1 + static_cast<size_t>(nranks))));
+  // the all-gather writes one record block per rank of the communicator
+  const tg_nccl_count_fn count = nccl_comm_count();
+  if (count) {
+    int n = 0;
+    const int cr = count(nccl_comm, &n);
+    if (cr != 0) return fail(TG_ERR_CUDA, "ncclCommCount failed (ncclResult_t " + std::to_string(cr) + ")");
+    if (n != nranks) return fail(TG_ERR_INVALID_ARG, "nranks differs from the communicator's size");
   }
+  const size_t rec = sizeof(tg_shard_record) * static_cast<size_t>(batch);
+  // one lock from the buffer check to the merge launch: the record buffer is
+  // the handle's, shared by every call on it
+  std::lock_guard<std::mutex> lk(s->mu);
+  if (rec * (1 + static_cast<size_t>(nranks)) > s->shard_recs.cap)
+    return fail(TG_ERR_UNSUPPORTED, "shard records not reserved for this batch and nranks (call tg_sampler_reserve)");
   tg_shard_record* local = static_cast<tg_shard_record*>(s->shard_recs.p);
   tg_shard_record* all = local + batch;
   int32_t rc = launch_sample(s, vocab_offset, full_vocab, local, logits, dtype, row_stride, batch, params,
@@ -516,7 +569,29 @@ int32_t tg_sample_sharded(tg_sampler* s, void* nccl_comm, int32_t nranks, int32_
   DeviceGuard g(s->device);
   const int nr = allgather(local, all, rec, 1 /* ncclUint8 */, nccl_comm, static_cast<cudaStream_t>(stream));
   if (nr != 0) return fail(TG_ERR_CUDA, "ncclAllGather failed (ncclResult_t " + std::to_string(nr) + ")");
+  if (s->coll_timeout_ms > 0) {  // bounded wait for the collective; on expiry the communicator is aborted
+    rc = wait_collective(s, nccl_comm, static_cast<cudaStream_t>(stream));
+    if (rc != TG_OK) return rc;
+  }
   return tg_sample_shard_merge(s, all, nranks, full_vocab, batch, params, uniforms, out_ids, out_probs, stream);
+}
+
+int32_t tg_sampler_reserve(tg_sampler* s, int32_t max_K, int32_t max_ranks) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (max_K < 0 || max_K > 64 || max_ranks < 0) return fail(TG_ERR_INVALID_ARG, "max_K outside [0, 64] or max_ranks < 0");
+  std::lock_guard<std::mutex> lk(s->mu);
+  DeviceGuard g(s->device);
+  const size_t B = static_cast<size_t>(s->max_batch);
+  TG_CUDA(s->stats.ensure(sizeof(tg::SpecStat) * B * (2 * static_cast<size_t>(max_K) + 1) + sizeof(int32_t) * 2 * B));
+  if (max_ranks > 0) TG_CUDA(s->shard_recs.ensure(sizeof(tg_shard_record) * B * (1 + static_cast<size_t>(max_ranks))));
+  return TG_OK;
+}
+
+int32_t tg_sampler_set_collective_timeout(tg_sampler* s, int32_t timeout_ms) {
+  if (!s) return fail(TG_ERR_INVALID_ARG, "sampler is NULL");
+  if (timeout_ms < 0) return fail(TG_ERR_INVALID_ARG, "timeout_ms < 0");
+  s->coll_timeout_ms = timeout_ms;
+  return TG_OK;
 }
 
 int32_t tg_sample_host(tg_sampler* s, const void* logits, int32_t dtype, int64_t row_stride,
@@ -601,12 +676,14 @@ static int32_t spec_verify_impl(tg_sampler* s, const void* target_logits, const 
   if (batch == 0) return TG_OK;
   if (!target_logits || !temperature || !out_ids || !out_n || (K > 0 && !draft_ids))
     return fail(TG_ERR_INVALID_ARG, "target_logits, draft_ids, temperature, out_ids and out_n are required");
-  if (K > 0 && (!draft_logits || !u_accept)) return fail(TG_ERR_INVALID_ARG, "draft_logits and u_accept are required when K > 0");
+  if (K > 0 && (draft_logits == nullptr) != (u_accept == nullptr))
+    return fail(TG_ERR_INVALID_ARG, "draft_logits and u_accept are given together or not at all");
   if (!u_draw) return fail(TG_ERR_INVALID_ARG, "u_draw is required");
   std::lock_guard<std::mutex> lk(s->mu);
   DeviceGuard g(s->device);
   const size_t nst = sizeof(tg::SpecStat) * static_cast<size_t>(batch) * (2 * K + 1);
-  TG_CUDA(s->stats.ensure(nst + sizeof(int32_t) * 2 * static_cast<size_t>(batch)));
+  if (nst + sizeof(int32_t) * 2 * static_cast<size_t>(batch) > s->stats.cap)
+    return fail(TG_ERR_UNSUPPORTED, "verification statistics not reserved for this batch and K (call tg_sampler_reserve)");
   tg::SpecArgs a{target_logits, draft_logits, batch, K, s->vocab, draft_ids, temperature,
                  u_accept, u_draw, out_ids, out_n, static_cast<tg::SpecStat*>(s->stats.p),
                  s->d_status};
@@ -653,8 +730,10 @@ int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_
   if (static_cast<int64_t>(batch) * (2 * K + 1) > TG_STATIC_SPEC_MAX_ROWS)
     return fail(TG_ERR_UNSUPPORTED, "batch * (2K + 1) exceeds TG_STATIC_SPEC_MAX_ROWS (the static scratch)");
   if (batch == 0) return TG_OK;
-  if (!target_logits || !temperature || !out_ids || !out_n || !u_draw || (K > 0 && (!draft_ids || !draft_logits || !u_accept)))
+  if (!target_logits || !temperature || !out_ids || !out_n || !u_draw || (K > 0 && !draft_ids))
     return fail(TG_ERR_INVALID_ARG, "missing required pointer");
+  if (K > 0 && (draft_logits == nullptr) != (u_accept == nullptr))
+    return fail(TG_ERR_INVALID_ARG, "draft_logits and u_accept are given together or not at all");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev || device >= kMaxDevices)
     return fail(TG_ERR_NO_DEVICE, "CUDA device not present");
@@ -671,6 +750,22 @@ int32_t tg_spec_verify_static(int32_t device, int32_t vocab, const void* target_
   const cudaError_t le = dtype == TG_DTYPE_F32 ? tg::launch_spec<0>(a, st) : tg::launch_spec<1>(a, st);
   if (le == cudaErrorInvalidValue) return fail(TG_ERR_UNSUPPORTED, "vocab too large for the staged verification (vocab * element size > 1.6 MB)");
   TG_CUDA(le);
+  return TG_OK;
+}
+
+int32_t tg_spec_verify_static_status(int32_t device, uint32_t* out_bits) {
+  if (!out_bits) return fail(TG_ERR_INVALID_ARG, "out_bits is NULL");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev || device >= kMaxDevices)
+    return fail(TG_ERR_NO_DEVICE, "CUDA device not present");
+  DeviceGuard g(device);
+  void* scratch = nullptr;
+  TG_CUDA(static_scratch(device, &scratch));
+  uint32_t* status = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) +
+                                                 TG_STATIC_SPEC_MAX_ROWS * sizeof(tg::SpecStat));
+  TG_CUDA(cudaDeviceSynchronize());
+  TG_CUDA(cudaMemcpy(out_bits, status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  TG_CUDA(cudaMemset(status, 0, sizeof(uint32_t)));
   return TG_OK;
 }
 

@@ -82,6 +82,22 @@ class Sampler:
     def handle(self):
         return self._h
 
+    def reserve(self, max_K: int = 0, max_ranks: int = 0) -> None:
+        """tg_sampler_reserve: buffers for tg_spec_verify of up to max_K proposals
+        and tg_sample_sharded of up to max_ranks ranks at max_batch rows.  The
+        wrappers below call it when a call needs more than was reserved; call it
+        up front to keep every later call allocation-free."""
+        k = max(max_K, getattr(self, "_res_K", -1))
+        r = max(max_ranks, getattr(self, "_res_ranks", 0))
+        if k == getattr(self, "_res_K", -1) and r == getattr(self, "_res_ranks", 0):
+            return
+        check(self._L.tg_sampler_reserve(self._h, max(k, 0), r))
+        self._res_K, self._res_ranks = max(k, 0), r
+
+    def set_collective_timeout(self, ms: int) -> None:
+        """Deadline of tg_sample_sharded's all-gather (0: no host wait)."""
+        check(self._L.tg_sampler_set_collective_timeout(self._h, int(ms)))
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             self._L.tg_sampler_destroy(self._h)
@@ -150,7 +166,9 @@ class Sampler:
 
     def spec_verify(self, target_logits, draft_logits, draft_ids, temperature, u_accept, u_draw,
                     *, out=None, out_n=None, stream=None):
-        """tg_spec_verify on device tensors.  target [B, K+1, V], draft [B, K, V]."""
+        """tg_spec_verify on device tensors.  target [B, K+1, V], draft [B, K, V]
+        (draft_logits and u_accept None: greedy verification without a draft,
+        Medusa / EAGLE style)."""
         B, K1, V = target_logits.shape
         K = K1 - 1
         if V != self.vocab:
@@ -160,6 +178,7 @@ class Sampler:
             out = torch.empty((B, K + 1), dtype=torch.int32, device=dev)
         if out_n is None:
             out_n = torch.empty(B, dtype=torch.int32, device=dev)
+        self.reserve(max_K=K)
         check(self._L.tg_spec_verify(self._h, _ptr(target_logits), _ptr(draft_logits),
                                      _dtype_code(target_logits), B, K, _ptr(draft_ids),
                                      _ptr(temperature), _ptr(u_accept), _ptr(u_draw), _ptr(out),
@@ -178,6 +197,7 @@ class Sampler:
             out = torch.empty((B, K + 1), dtype=torch.int32, device=dev)
         if out_n is None:
             out_n = torch.empty(B, dtype=torch.int32, device=dev)
+        self.reserve(max_K=K)
         check(self._L.tg_spec_verify_masked(self._h, _ptr(target_logits), _ptr(draft_logits),
                                             _dtype_code(target_logits), B, K, _ptr(draft_ids),
                                             _ptr(temperature), _ptr(u_accept), _ptr(u_draw),
@@ -233,6 +253,7 @@ class Sampler:
             out = torch.empty(B, dtype=torch.int32, device=dev)
         hstride = history.shape[1] if history is not None else 0
         nstates = mask_table.shape[0] if mask_table is not None else 0
+        self.reserve(max_ranks=nranks)
         check(self._L.tg_sample_sharded(self._h, ctypes.c_void_p(int(nccl_comm)), nranks, vocab_offset,
                                         full_vocab, _ptr(logits), _dtype_code(logits), logits.stride(0), B,
                                         _ptr(params), _ptr(history), _ptr(history_len), hstride,
