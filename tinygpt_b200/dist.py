@@ -43,21 +43,48 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
     return float(t.item())
 
 
-def sample_vocab_sharded(sampler, logits_shard, params, vocab_offset: int, full_vocab: int, *,
-                         uniforms, history=None, history_len=None, mask_table=None,
-                         state_id=None, out_probs=None, group=None):
-    """Vocab-sharded sampling: this rank holds ids [vocab_offset, +shard width) of
-    every row.  Local records -> NCCL all-gather over NVLink -> identical merge on
-    every rank; returns the ids of the whole rows (what tg_sample returns on
-    them)."""
+class CollectiveError(RuntimeError):
+    """The record exchange of the vocab-sharded mode failed or missed its
+    deadline (a rank that left, a broken link)."""
+
+
+def exchange_records(rec, group=None, timeout_s: float | None = None):
+    """All-gather of the per-row records of every rank: [world, *rec.shape].
+    With timeout_s the wait is bounded; a rank that never joins (or left) then
+    ends the call with CollectiveError within about timeout_s instead of
+    blocking the caller."""
+    import datetime
+
     import torch
     import torch.distributed as dist
+    world = dist.get_world_size(group)
+    # concatenated along dim 0 (the layout every backend accepts), viewed per rank
+    flat = torch.empty((world * rec.shape[0],) + tuple(rec.shape[1:]), dtype=rec.dtype, device=rec.device)
+    gathered = flat.view((world,) + tuple(rec.shape))
+    try:
+        work = dist.all_gather_into_tensor(flat, rec, group=group, async_op=True)
+        if timeout_s is None:
+            work.wait()
+        elif not work.wait(timeout=datetime.timedelta(seconds=timeout_s)):
+            raise CollectiveError(f"record exchange did not complete within {timeout_s} s")
+    except CollectiveError:
+        raise
+    except Exception as e:  # noqa: BLE001 - the backend's own failure (peer gone, timeout)
+        raise CollectiveError(f"record exchange failed: {e}") from e
+    return gathered
+
+
+def sample_vocab_sharded(sampler, logits_shard, params, vocab_offset: int, full_vocab: int, *,
+                         uniforms, history=None, history_len=None, mask_table=None,
+                         state_id=None, out_probs=None, group=None, timeout_s: float | None = None):
+    """Vocab-sharded sampling: this rank holds ids [vocab_offset, +shard width) of
+    every row.  Local records -> all-gather over NVLink -> identical merge on
+    every rank; returns the ids of the whole rows (what tg_sample returns on
+    them).  timeout_s bounds the exchange (CollectiveError on expiry)."""
     rec = sampler.sample_shard_local(logits_shard, params, vocab_offset, full_vocab,
                                      history=history, history_len=history_len,
                                      mask_table=mask_table, state_id=state_id)
-    world = dist.get_world_size(group)
-    gathered = torch.empty((world,) + tuple(rec.shape), dtype=rec.dtype, device=rec.device)
-    dist.all_gather_into_tensor(gathered, rec, group=group)
+    gathered = exchange_records(rec, group=group, timeout_s=timeout_s)
     ids, probs = sampler.sample_shard_merge(gathered, full_vocab, params, uniforms=uniforms,
                                             out_probs=out_probs)
     return ids, probs
