@@ -41,3 +41,21 @@ def sampler_factory(cuda_lib):
             cache[key] = Sampler(vocab, max_batch, 0)
         return cache[key]
     return make
+
+
+# Parity pins report what they exempted (draws near a cumulative boundary,
+# probabilities below the mass quantum); the counts are printed at the end of
+# the run, visible under -q too.
+PIN_REPORT: list[str] = []
+
+
+@pytest.fixture
+def pin_report():
+    return PIN_REPORT
+
+
+def pytest_terminal_summary(terminalreporter):
+    if PIN_REPORT:
+        terminalreporter.section("parity pin exemptions")
+        for line in PIN_REPORT:
+            terminalreporter.write_line(line)

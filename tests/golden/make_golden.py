@@ -8,10 +8,17 @@ tree is mounted; the fixtures travel, the reference does not).
                       (wasm/src/model.cpp:473-522, via oracle/_ref/libtgref.so)
                       samples from chosen logits, with the canonical uniforms its
                       std::mt19937 stream produced.
+  ref_python_ref_configs.npz
+                      the same capture at the configurations' shapes: V=50257
+                      (config 1: T 0.8, top-k 40, five ids boosted +8), V=32000
+                      bf16 with a Zipf bias and no top-k (config 2's T 0.7), and
+                      V=128256 bf16 with a Zipf bias (config 4's T and top-k
+                      range, bf16 ties at the threshold).
   oracle_cases.npz    oracle outputs (ids, probs) for seeded workloads of the
                       five configurations, regenerated from their seeds in tests.
 
-Usage: python tests/golden/make_golden.py [--reference /root/reference]
+Usage: python tests/golden/make_golden.py --reference <sarthak-fleet/tinygpt tree>
+(or set TG_REFERENCE_ROOT)
 """
 from __future__ import annotations
 
@@ -78,7 +85,8 @@ def python_ref_probs(mod, logits: np.ndarray, temperature: float, top_k):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TG_REFERENCE_ROOT"),
+                    required="TG_REFERENCE_ROOT" not in os.environ)
     args = ap.parse_args()
     oracle.build()
     g = W.rng(20261201)
@@ -136,7 +144,46 @@ def main() -> None:
         out[f"spec_ids_{c}_{seed}_{B}"] = o
         out[f"spec_n_{c}_{seed}_{B}"] = n
     np.savez_compressed(os.path.join(HERE, "oracle_cases.npz"), **out)
+    python_ref_config_pins(mod)
     print("golden fixtures written to", HERE)
+
+
+def zipf_bias(g, V: int) -> np.ndarray:
+    """-1.1 * ln(rank) over a random permutation of the ids (the bias of
+    configs 2 and 4, tinygpt_b200.workloads)."""
+    perm = g.permutation(V)
+    bias = np.empty(V, np.float32)
+    bias[perm] = (-1.1 * np.log(np.arange(1, V + 1, dtype=np.float64))).astype(np.float32)
+    return bias
+
+
+def python_ref_config_pins(mod) -> None:
+    """python_ref's probabilities at the configurations' shapes (a few rows each)."""
+    g = W.rng(20261202)
+    cases = []
+    # config 1: V=50257 fp32, N(0, 3^2) + 8 on five ids, T 0.8, top-k 40
+    x = g.normal(0.0, 3.0, size=(2, 50257)).astype(np.float32)
+    for r in range(2):
+        x[r, g.choice(50257, 5, replace=False)] += 8.0
+    cases.append(dict(name="config1", logits=x, T=0.8, k=40, bf16=False))
+    # config 2 shape: V=32000 bf16, N(0, 2.5^2) + Zipf bias, T 0.7, no top-k
+    x = np.stack([g.normal(0.0, 2.5, size=32000).astype(np.float32) + zipf_bias(g, 32000) for _ in range(2)])
+    cases.append(dict(name="config2", logits=W.bf16_bits_to_f32(W.to_bf16_bits(x)), T=0.7, k=None, bf16=True))
+    # config 4 shape: V=128256 bf16, N(0, 3^2) + Zipf bias; k and T at both ends of config 4's ranges
+    for T, k in ((0.3, 1), (0.9, 50), (1.2, 1024)):
+        x = (g.normal(0.0, 3.0, size=128256).astype(np.float32) + zipf_bias(g, 128256))[None]
+        cases.append(dict(name=f"config4_T{T}_k{k}", logits=W.bf16_bits_to_f32(W.to_bf16_bits(x)), T=T, k=k,
+                          bf16=True))
+    out = {"n": len(cases)}
+    for i, c in enumerate(cases):
+        pr = python_ref_probs(mod, c["logits"], c["T"], c["k"])
+        out[f"name_{i}"] = np.array(c["name"])
+        out[f"logits_{i}"] = W.to_bf16_bits(c["logits"]) if c["bf16"] else c["logits"]
+        out[f"bf16_{i}"] = np.int32(c["bf16"])
+        out[f"T_{i}"] = np.float32(c["T"])
+        out[f"k_{i}"] = np.int32(0 if c["k"] is None else c["k"])
+        out[f"probs_{i}"] = pr
+    np.savez_compressed(os.path.join(HERE, "ref_python_ref_configs.npz"), **out)
 
 
 if __name__ == "__main__":

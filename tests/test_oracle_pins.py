@@ -31,26 +31,63 @@ def test_exp_within_one_ulp_of_libm(oracle_mod):
     assert oracle_mod.qmass(-40.0) == 0 and oracle_mod.qmass(float("-inf")) == 0
 
 
-def test_python_ref_distribution_pinned(oracle_mod):
-    """Support and probabilities equal the reference's softmax after top-k:
-    support exactly, probabilities within 1e-5 relative plus the 2^-44
-    fixed-point quantum of the build's mass definition."""
+# Probabilities are q / S with q = trunc(e * 2^44) and S >= 2^44, so each one
+# carries an absolute error below 2^-44 from the fixed-point masses: the 1e-5
+# relative bound holds for every probability >= 2^-44 / 1e-5 (5.7e-9); below
+# that floor a probability is compared to within two quanta and counted.
+P_FLOOR = 2.0 ** -44 / 1e-5
+
+
+def _check_python_ref(oracle_mod, x, T, k, pref, what, report):
+    _, _, _, st, q = oracle_mod.sample_row_detail(x, params1(T, k))
+    keep = (st & 1).astype(bool)
+    assert np.array_equal(keep, pref > 0), f"{what}: top-k support differs"
+    p = q.astype(np.float64) / q.sum(dtype=np.float64)
+    pr = pref.astype(np.float64)
+    big = pr >= P_FLOOR
+    rel = np.abs(p[big] - pr[big]) / pr[big]
+    assert rel.max(initial=0.0) <= 1e-5, f"{what}: relative error {rel.max()}"
+    small = keep & ~big
+    assert (np.abs(p[small] - pr[small]) <= 2.0 ** -43).all(), f"{what}: error below the quantum floor"
+    report[0] += int(big.sum())
+    report[1] += int(small.sum())
+    report[2] = max(report[2], float(rel.max(initial=0.0)))
+
+
+def test_python_ref_distribution_pinned(oracle_mod, pin_report):
+    """Support exactly and probabilities within 1e-5 relative of the reference's
+    softmax after top-k (python_ref/model.py:213-224)."""
     z = np.load(os.path.join(GOLD, "ref_python_ref.npz"))
+    acc = [0, 0, 0.0]
     for i in range(int(z["n"])):
         x, T, k, pref = z[f"logits_{i}"], float(z[f"T_{i}"]), int(z[f"k_{i}"]), z[f"probs_{i}"]
         for r in range(x.shape[0]):
-            _, _, _, st, q = oracle_mod.sample_row_detail(x[r], params1(T, k))
-            keep = (st & 1).astype(bool)
-            assert np.array_equal(keep, pref[r] > 0), f"case {i} row {r}: top-k support differs"
-            p = q.astype(np.float64) / q.sum(dtype=np.float64)
-            err = np.abs(p - pref[r]) - (1e-5 * pref[r] + 2.0 ** -40)
-            assert err.max() <= 0, f"case {i} row {r}: prob error {err.max()}"
+            _check_python_ref(oracle_mod, x[r], T, k, pref[r], f"python_ref case {i} row {r}", acc)
+    pin_report.append(f"python_ref small cases: {acc[0]} probabilities within 1e-5 relative (max {acc[2]:.2e}), "
+                      f"{acc[1]} below {P_FLOOR:.1e} within 2^-43")
 
 
-def test_wasm_tg_generate_draws_pinned(oracle_mod):
+def test_python_ref_pinned_at_config_shapes(oracle_mod, pin_report):
+    """The same pin at the configurations' vocabularies: V=50257 (config 1),
+    32000 and 128256 with bf16 ties at the top-k threshold."""
+    z = np.load(os.path.join(GOLD, "ref_python_ref_configs.npz"))
+    acc = [0, 0, 0.0]
+    for i in range(int(z["n"])):
+        x = z[f"logits_{i}"]
+        if int(z[f"bf16_{i}"]):
+            x = W.bf16_bits_to_f32(x)
+        T, k, pref = float(z[f"T_{i}"]), int(z[f"k_{i}"]), z[f"probs_{i}"]
+        for r in range(x.shape[0]):
+            _check_python_ref(oracle_mod, x[r], T, k, pref[r], f"python_ref {z[f'name_{i}']} row {r}", acc)
+    pin_report.append(f"python_ref config shapes: {acc[0]} probabilities within 1e-5 relative (max {acc[2]:.2e}), "
+                      f"{acc[1]} below {P_FLOOR:.1e} within 2^-43")
+
+
+def test_wasm_tg_generate_draws_pinned(oracle_mod, pin_report):
     """Same ids as the reference's C++ tg_generate for the same logits and the
-    same uniform stream; draws whose point lies within 1e-5 of a cumulative
-    boundary are exempt (summation order differs) and counted."""
+    same uniform stream.  Its fp32 running sums and the exact masses here differ
+    by rounding, so a draw whose point lies within 1e-6 (relative to the total)
+    of a cumulative boundary is exempt; exempt draws are counted and reported."""
     z = np.load(os.path.join(GOLD, "ref_wasm.npz"))
     checked = exempt = 0
     for r in range(z["logits"].shape[0]):
@@ -65,11 +102,14 @@ def test_wasm_tg_generate_draws_pinned(oracle_mod):
             if T > 0:
                 S = int(q[(st & 2).astype(bool)].sum())
                 cdf = np.cumsum(np.where((st & 2).astype(bool), q, 0)).astype(np.float64)
-                if np.min(np.abs(cdf - u * S)) < 1e-5 * S:
+                if np.min(np.abs(cdf - u * S)) < 1e-6 * S:
                     exempt += 1
+                    pin_report.append(f"wasm row {r} step {s}: draw point within 1e-6 of a boundary "
+                                      f"(oracle {i}, reference {want})")
                     continue
             checked += 1
             assert i == want, f"row {r} step {s}: oracle {i} reference {want}"
+    pin_report.append(f"wasm tg_generate: {checked} draws equal, {exempt} exempt")
     assert checked > 1000 and exempt < 0.01 * checked
 
 
