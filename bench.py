@@ -42,7 +42,7 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
-def make_inputs_gpu(torch, dev, seed):
+def make_inputs_gpu(torch, dev, seed, B=B):
     """Config-4 inputs built on the device: N(0,3^2) + Zipf(1.1) bias over a
     per-row affine permutation, k~U{1..1024}, p~U[0.5,1], T~U[0.3,1.2],
     repetition 1.05 over 512 Zipf history ids."""
@@ -83,6 +83,8 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        if not self.gpus:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={','.join(map(str, self.gpus))}", f"--query-gpu={self.Q}",
@@ -282,8 +284,89 @@ def run_config(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "algorithmic_bytes_per_call": bytes_call,
                          "peak_source": peak_kind}}
+    if cfg == 3:  # the 64 mask rows are read from L2 after the first touch: count the table once per call
+        once = Vc * 4 * Bc + sets[0]["mask_table"].nbytes
+        a1 = once / (us * 1e-6) / 1e9
+        line["roofline_mask_table_once"] = {"achieved": a1, "frac": a1 / peak, "algorithmic_bytes_per_call": once,
+                                            "note": "logits per row + the whole mask table once"}
     print(json.dumps(line), flush=True)
     s.close()
+
+
+def vocab_sharded_leg(torch, dist, s_full, dev, rank, world, local, args, steps=20):
+    """tg_sample_sharded over the job's ranks: every rank holds a 1/world slice of
+    the SAME config-4 rows, one NCCL all-gather of per-row records, identical
+    merge on every rank.  Returns rows/s of the whole job (B rows per call), and
+    whether the ids equal tg_sample on the whole rows on every rank."""
+    from tinygpt_b200.dist import NcclComm
+    from tinygpt_b200.sampler import Sampler, params_to_device
+    if V % world:
+        return {"skipped": f"vocab {V} not divisible by {world}"}
+    w = make_inputs_gpu(torch, dev, 4242)  # the same seed on every rank: the same rows
+    width = V // world
+    v0 = rank * width
+    shard = w["logits"][:, v0:v0 + width].contiguous()
+    p = params_to_device(w["params"], dev)
+    hist = torch.from_numpy(w["history"]).to(dev)
+    hlen = torch.from_numpy(w["history_len"]).to(dev)
+    u = torch.from_numpy(w["uniforms"]).to(dev)
+    ref, _ = s_full.sample(w["logits"], p, history=hist, history_len=hlen, uniforms=u)
+    comm = NcclComm(rank, world, local)
+    ss = Sampler(width, B, local)
+    ss.reserve(max_ranks=world)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    call = lambda: ss.sample_sharded(comm.ptr, world, shard, p, v0, V, history=hist, history_len=hlen,  # noqa: E731
+                                     uniforms=u, out=out)
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    same = torch.tensor([int(torch.equal(out, ref))], device=dev)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / steps
+    ss.close()
+    comm.close()
+    return {"rows_per_s": B / (ms / 1e3), "ms_per_call": ms, "rows_per_call": B, "shards": world,
+            "ids_equal_batch_mode": bool(same.item()),
+            "note": "each rank holds V/N ids of the same rows; local top-k records, one ncclAllGather, merge"}
+
+
+def batch_8192_leg(torch, dev, local, args, steps=20):
+    """Config 4 at its larger batch (8192 rows: two launch pairs of 4096)."""
+    from tinygpt_b200.sampler import Sampler, params_to_device
+    Bb = 8192
+    w = make_inputs_gpu(torch, dev, 8192, B=Bb)
+    s = Sampler(V, Bb, local)
+    p = params_to_device(w["params"], dev)
+    hist = torch.from_numpy(w["history"]).to(dev)
+    hlen = torch.from_numpy(w["history_len"]).to(dev)
+    u = torch.from_numpy(w["uniforms"]).to(dev)
+    out = torch.empty(Bb, dtype=torch.int32, device=dev)
+    call = lambda: s.sample(w["logits"], p, history=hist, history_len=hlen, uniforms=u, out=out)  # noqa: E731
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    s.close()
+    del w
+    peak, _ = measured_peak()
+    gbs = Bb * BYTES_PER_ROW / (ms / 1e3) / 1e9
+    return {"rows_per_s": Bb / (ms / 1e3), "ms_per_call": ms, "steps": steps,
+            "step_frac_of_peak": gbs / peak, "note": "2.1 GB of logits per call, the L2 holds none of it"}
 
 
 def main():
@@ -349,8 +432,13 @@ def main():
         step(i)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(list(range(world)) if rank == 0 else [local]) as clk:
-        time.sleep(0.5)  # let the sampler start
+    # one nvidia-smi sampler per node (rank 0, every GPU of the job); the clock
+    # record spans the timed steps and 0.5 s of the same steps right after them,
+    # so it holds samples even when the timed region is a few milliseconds
+    sampler_gpus = list(range(world)) if rank == 0 else []
+    with ClockSampler(sampler_gpus) as clk:
+        if sampler_gpus:
+            time.sleep(0.5)  # let the sampler start
         barrier()
         tw0 = time.time()
         e0.record(stream)
@@ -358,8 +446,16 @@ def main():
             step(i)
         e1.record(stream)
         barrier()
+        ms = e0.elapsed_time(e1)
+        t_end = time.time() + 0.5
+        i = 0
+        while time.time() < t_end:
+            for _ in range(20):
+                step(i)
+                i += 1
+            torch.cuda.synchronize()
+        barrier()
         tw1 = time.time()
-    ms = e0.elapsed_time(e1)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -401,13 +497,27 @@ def main():
     t0 = time.perf_counter()
     for _ in range(args.e2e_steps):
         o, _ = s.sample_host(hl, hp, history=hh, history_len=hn, uniforms=hu)
-    dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    e2e_local_s = time.perf_counter() - t0
+    dt = torch.tensor([e2e_local_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(dt, op=dist.ReduceOp.MAX)
     e2e_val = B * args.e2e_steps * world / float(dt.item())
     h2d = B * V * 2 + B * 32 + B * HIST * 4 + B * 4 + B * 4
     d2h = B * 4
     del hout
+
+    # per-rank figures (the max over ranks decides `value`; these name the slow rank)
+    mine = torch.tensor([ms / args.steps] + kms + [h2d * args.e2e_steps / e2e_local_s / 1e9],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+    else:
+        allr = [mine]
+    per_rank = [{"rank": r, "ms_per_step": float(x[0]), "kernel_ms": [float(v) for v in x[1:-1]],
+                 "e2e_h2d_gbs": float(x[-1])} for r, x in enumerate(allr)]
+    vsh = vocab_sharded_leg(torch, dist, s, dev, rank, world, local, args) if world > 1 else None
+    b8192 = batch_8192_leg(torch, dev, local, args) if world == 1 else None
 
     cpu = None
     if rank == 0 and world == 1:
@@ -443,9 +553,14 @@ def main():
             "e2e": {"value": e2e_val, "unit": "rows/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                     "path": "tg_sample_host, pinned host buffers"},
-            "gpu_launches": args.steps * nk,
-            "clocks": clocks,
+            "gpu_launches": args.steps * (3 if nk == 2 else 1),
+            "clocks": dict(clocks, window="the timed steps + 0.5 s of the same steps right after them"),
+            "per_rank": per_rank,
         }
+        if vsh:
+            line["vocab_sharded"] = vsh
+        if b8192:
+            line["b8192"] = b8192
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)

@@ -1474,6 +1474,28 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
     }
     pc.mark(2);
     if constexpr (kStream) {
+      // fewer than k raw candidates: the threshold was too high.  Lower it here
+      // (a 4x deeper rank of the sample, the row re-read while it is likely
+      // still in L2), where the retry overlaps the other rows' streams, rather
+      // than leaving the row to a lone fallback CTA after the finisher.
+      for (int attempt = 0; attempt < kRetries && sm.cand_count < static_cast<int>(need) && theta > neg_inf();
+           attempt++) {
+        rk = rk * 4u;
+        float vm[SV];
+#pragma unroll
+        for (int q = 0; q < SV; q++) {
+          const int j = t + q * NT;
+          vm[q] = j < nvec ? vmax_of(__ldg(vrow + j), j) : neg_inf();
+        }
+        float nt = sample_theta<SV, NT>(vm, rk, sm);
+        if (!(nt < theta)) nt = neg_inf();
+        theta = nt;
+        if (t == 0) sm.cand_count = 0;
+        __syncthreads();
+        scalars(theta);
+        scan(theta, 0);
+        fits = expand(theta);
+      }
       if (t == 0) {
         a.cand_gn[b] = sm.cand_count;
         a.cand_gth[b] = theta;
