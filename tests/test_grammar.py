@@ -446,3 +446,79 @@ def test_draft_state_rows():
     assert rows[1, 0] == expect0[0] and rows[1, 1] == expect0[1]
     assert list(rows[1, 2:]) == [rows[1, 1]] * 3
     assert s0.row() == expect0[0] and s1.row() == expect0[0]
+
+
+# ------------------------------------------------------------------ the reference's own grammars
+# tests/golden/grammars/ holds the grammars the reference serves (its grammars/
+# directory: the pace-fm-* JSON Schemas and pace-tool-tags.gbnf), as fixtures.
+
+REF_GRAMMARS = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "grammars")
+REF_SCHEMAS = sorted(f for f in os.listdir(REF_GRAMMARS) if f.endswith(".schema.json"))
+
+
+def schema_vocab(rng, schema: dict, n=700):
+    """synthetic_vocab plus the schema's own key names, enum members and their
+    quoted forms, so multi-byte tokens cross the structure of its documents."""
+    pieces = set(synthetic_vocab(rng, n))
+
+    def walk(node):
+        if isinstance(node, dict):
+            for k, v in node.get("properties", {}).items():
+                pieces.update({k.encode(), ('"' + k + '"').encode(), ('"' + k + '":').encode()})
+                walk(v)
+            for e in node.get("enum", []):
+                if isinstance(e, str):
+                    pieces.update({e.encode(), ('"' + e + '"').encode(), e[:3].encode()})
+            if "items" in node:
+                walk(node["items"])
+    walk(schema)
+    pieces.discard(b"")
+    vocab = sorted(pieces)
+    vocab.insert(5, b"")
+    return vocab
+
+
+@pytest.mark.parametrize("name", REF_SCHEMAS)
+def test_reference_schemas_documents_and_masks(name):
+    text = open(os.path.join(REF_GRAMMARS, name)).read()
+    schema = json.loads(text)
+    node = go.parse_schema(schema)
+    rng = random.Random(sum(name.encode()))
+    g = native(text)
+    for _ in range(12):  # documents: acceptance and completion agree byte for byte
+        doc = gen_value(node, rng).encode()
+        n, o = g.state(), go.compile_schema(text)
+        assert n.accept_bytes(doc) and o.accept_bytes(doc), doc
+        assert n.is_complete and o.is_complete
+        cut = rng.randint(0, len(doc))
+        mut = doc[:cut] + bytes([rng.choice(b'{}[]",:0123456789ax ')])
+        n, o = g.state(), go.compile_schema(text)
+        assert n.accept_bytes(mut) == o.accept_bytes(mut), mut
+    vocab = schema_vocab(rng, schema)
+    gv = Grammar(text, vocab, eos_id=3)
+    for _ in range(3):  # masks over a multi-byte vocabulary along valid documents
+        doc = gen_value(node, rng).encode()
+        for cut in sorted({0, len(doc)} | {rng.randint(0, len(doc)) for _ in range(4)}):
+            n, o = gv.state(), go.compile_schema(text)
+            assert n.accept_bytes(doc[:cut]) and o.accept_bytes(doc[:cut])
+            assert list(n.allowed()) == go.mask_ids(o, vocab, eos_id=3), (name, doc[:cut])
+
+
+def test_reference_tool_tag_grammar():
+    text = open(os.path.join(REF_GRAMMARS, "pace-tool-tags.gbnf")).read()
+    g = native(text)
+    assert g.kind == 1  # the tool-tag grammar
+    for doc in TAG_DOCS:
+        raw = doc.encode()
+        n, o = g.state(), go.PaceToolTagFSM()
+        assert n.accept_bytes(raw) == o.accept_bytes(raw), raw
+        assert n.is_complete == o.is_complete, raw
+    heads = [b"[POINT:", b"[POINT:none]", b"[CLICK:", b"[TYPE:", b"[SCROLL:", b"[KEY:", b"[OPEN_APP:"]
+    vocab = sorted(set(BYTE_VOCAB) | set(heads) | {b"none]", b"up:", b"12", b",3", b"ab]", b"Safari", b"Look ",
+                                                     b"here ", b"the ", b"button"})
+    gv = Grammar(text, vocab)
+    for prefix in [b"", b"Look here ", b"Look here [", b"Look here [CLICK:12,3", b"ok [SCROLL:up:1",
+                   b"typing [TYPE:Hi", b"go [OPEN_APP:Saf"]:
+        n, o = gv.state(), go.PaceToolTagFSM()
+        assert n.accept_bytes(prefix) == o.accept_bytes(prefix), prefix
+        assert list(n.allowed()) == go.mask_ids(o, vocab), prefix
