@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kFuFinTid0 + 4 * 32 * kFuG, 1) sample_fused_ke
   // a vector of -inf (outside the row)
   const uint4 kNegVec = DT == 1 ? make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u)
                                 : make_uint4(0xff800000u, 0xff800000u, 0xff800000u, 0xff800000u);
-  extern __shared__ __align__(128) unsigned char dyn[];
+  extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ FusedCtl ctl;
   const int tid = threadIdx.x;
   const int S = cfg.stages, NS = cfg.slots;

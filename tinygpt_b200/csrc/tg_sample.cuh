@@ -53,8 +53,14 @@ constexpr int kStreamCtasPerSm = TG_STREAM_CTAS;  // occupancy of the streaming 
 // Candidate target of the threshold: the sample estimates the element of rank
 // kTgtMul * k + kTgtAdd; the margin over k absorbs the sample's error (tighter
 // margins measured slower: more rows needed a second pass).
-constexpr float kTgtMul = 1.5f;
-constexpr float kTgtAdd = 96.0f;
+#ifndef TG_TGT_MUL
+#define TG_TGT_MUL 1.5f
+#endif
+#ifndef TG_TGT_ADD
+#define TG_TGT_ADD 96.0f
+#endif
+constexpr float kTgtMul = TG_TGT_MUL;
+constexpr float kTgtAdd = TG_TGT_ADD;
 constexpr int kRing = 64;  // hit-vector ring entries per warp (drained at 32)
 static_assert((kSampleNT / 32) * kRing * 20 <= kCandMax * 4, "rings must fit in cand_e");
 constexpr int kWideNT = 1024;  // threads per CTA for small batches
