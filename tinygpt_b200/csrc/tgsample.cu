@@ -376,7 +376,7 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
       else
         tg::sample_fused_kernel<1><<<grid, threads, fsmem, st>>>(c, fcfg);
       if (mark) TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
-      const int g = n < nsm * tg::kMinCtasPerSm ? n : nsm * tg::kMinCtasPerSm;
+      const int g = n;  // one CTA per possible fallback row
       if (dtype == TG_DTYPE_F32)
         tg::sample_list_kernel<0><<<g, tg::kSampleNT, smem, st>>>(c);
       else
@@ -405,7 +405,7 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
         tg::finish_warp_kernel<2><<<grid, rpc * 64, tg::kWfSmem, st>>>(c, pool);
       else
         tg::finish_warp_kernel<1><<<grid, rpc * 32, tg::kWfSmem, st>>>(c, pool);
-      const int g = n < nsm * tg::kMinCtasPerSm ? n : nsm * tg::kMinCtasPerSm;
+      const int g = n;  // one CTA per possible fallback row
       if (dtype == TG_DTYPE_F32)
         tg::sample_list_kernel<0><<<g, tg::kSampleNT, smem, st>>>(c);
       else
