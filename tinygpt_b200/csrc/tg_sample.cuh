@@ -40,6 +40,9 @@ constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold 
 #define TG_UNROLL 4
 #endif
 constexpr int kUnroll = TG_UNROLL;  // 128-bit loads in flight per thread
+#ifndef TG_THETA_PREFETCH
+#define TG_THETA_PREFETCH 8  // 128-bit vectors per thread prefetched to L2 while theta is computed
+#endif
 constexpr int kNoTopkTarget = 512;  // candidate target of rows without top-k
 constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) before the full row
 #ifndef TG_MIN_CTAS
@@ -62,6 +65,9 @@ constexpr int kStreamCtasPerSm = TG_STREAM_CTAS;  // occupancy of the streaming 
 constexpr float kTgtMul = TG_TGT_MUL;
 constexpr float kTgtAdd = TG_TGT_ADD;
 constexpr int kRing = 64;  // hit-vector ring entries per warp (drained at 32)
+// the streaming kernel's rings take up to a whole 4-vector warp group (128
+// entries) on top of fewer than 32 left over
+constexpr int kStreamRing = 160;
 static_assert((kSampleNT / 32) * kRing * 20 <= kCandMax * 4, "rings must fit in cand_e");
 constexpr int kWideNT = 1024;  // threads per CTA for small batches
 // Batches of kWideMinBatch..kWideMaxBatch rows run on wide CTAs (measured: a
@@ -126,6 +132,8 @@ struct SampleArgs {
   int32_t* fb_rows;
   int32_t* fb_count;
   int32_t debug_stop;  // diagnostics: the warp finisher leaves rows after this stage (0: off)
+  // streaming kernel: theta of every row is already in cand_gth (theta_kernel)
+  int32_t theta_given;
 };
 
 // History hash in shared memory: key = token id (-1 empty); val = count, then
@@ -1276,9 +1284,10 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
     uint4* rbase = reinterpret_cast<uint4*>(cand_e);
     if constexpr (!kStream && (NT / 32) * kRing * 20 > kCandMax * 4)
       rbase = reinterpret_cast<uint4*>(dyn + kCandMax * 12 + (ht ? static_cast<size_t>(8) * ht : 0));
-    uint4* rdata = rbase + warp * kRing;
-    int* ridx = reinterpret_cast<int*>(rbase + (NT / 32) * kRing) + warp * kRing;
-    auto drain = [&](int cnt, float th) {  // warp-uniform cnt <= kRing
+    constexpr int RING = kStream ? kStreamRing : kRing;
+    uint4* rdata = rbase + warp * RING;
+    int* ridx = reinterpret_cast<int*>(rbase + (NT / 32) * RING) + warp * RING;
+    auto drain = [&](int cnt, float th) {  // warp-uniform cnt <= RING
       __syncwarp();
       for (int i0 = 0; i0 < cnt; i0 += 32) {
         const int i = i0 + lane;
@@ -1337,7 +1346,42 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
         }
       };
       int jb = j0;
-      if (!mask) {
+      if (!mask && kStream) {
+        // full groups of the streaming kernel: each vector's maximum once, a
+        // 4-bit hit mask per thread and one warp prefix sum place the hit
+        // vectors in the ring (a warp group holds a hit ~85 % of the time on
+        // config 4, so a per-warp skip test rarely pays)
+        for (; jb + kUnroll * NT <= nvec; jb += kUnroll * NT) {
+          const uint4* pv = vrow + jb + t;
+          uint4 w[kUnroll];
+#pragma unroll
+          for (int q = 0; q < kUnroll; q++) w[q] = ldg_stream(pv + q * NT);
+          unsigned hm = 0;
+#pragma unroll
+          for (int q = 0; q < kUnroll; q++) hm |= (E::vmax(w[q]) >= th ? 1u : 0u) << q;
+          const int c = __popc(hm);
+          int incl = c;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += v;
+          }
+          const int total = __shfl_sync(kFull, incl, 31);
+          if (total) {
+            int pos = rcnt + incl - c;
+#pragma unroll
+            for (int q = 0; q < kUnroll; q++) {
+              if ((hm >> q) & 1u) {
+                rdata[pos] = w[q];
+                ridx[pos] = jb + q * NT + t;
+                pos++;
+              }
+            }
+            rcnt += total;
+            if (rcnt >= 32) { drain(rcnt, th); rcnt = 0; }
+          }
+        }
+      } else if (!mask) {
         // full groups: no bounds checks, and one packed max over the lane's
         // vectors decides whether the warp needs the exact per-vector test
         for (; jb + kUnroll * NT <= nvec; jb += kUnroll * NT) {
@@ -1446,6 +1490,16 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
       __syncthreads();
       fits = true;
       pc.mark(1);
+    } else if (kStream && a.theta_given) {
+      // theta from theta_kernel: the stream starts on its loads at once
+      if (V > kCandMax && sampled > 0) rk = rank_for(1.0f);
+      theta = a.cand_gth[b];
+      if (t == 0) sm.cand_count = 0;
+      __syncthreads();
+      pc.mark(1);
+      scalars(theta);
+      scan(theta, 0);
+      fits = expand(theta);
     } else {
       uint4 raw[SV];
       float vm[SV];
@@ -1455,6 +1509,17 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
         const int j = t + q * NT;
         if (j < nvec) raw[q] = ldg_stream(vrow + j);
       }
+#ifndef TG_NO_THETA_PREFETCH
+      // the streaming kernel computes theta next, with no loads of its own in
+      // flight: keep DRAM busy by pulling the row's next stages into L2
+      if constexpr (kStream) {
+#pragma unroll
+        for (int q = 0; q < TG_THETA_PREFETCH; q++) {
+          const int j = (SV + q) * NT + t;
+          if (j < nvec) asm volatile("prefetch.global.L2 [%0];" ::"l"(vrow + j));
+        }
+      }
+#endif
       // the history hash (counts only) is built while the sample loads fly
       if (!risers) build_hist(0.0f, false);
 #pragma unroll

@@ -19,6 +19,7 @@
 #include "tg_sample.cuh"
 #include "tg_finish_warp.cuh"
 #include "tg_fused.cuh"
+#include "tg_theta.cuh"
 #include "tg_spec.cuh"
 
 namespace {
@@ -351,7 +352,11 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
     fcfg.debug = dbg ? atoi(dbg) : 0;
   }
   const size_t fsmem = fused ? tg::fused_smem(fcfg.stages, fcfg.slots, fcfg.groups, a.ht_log2, nullptr) : 0;
-  const size_t ring_smem = static_cast<size_t>(tg::kSampleNT / 32) * tg::kRing * 20;
+  const size_t ring_smem = static_cast<size_t>(tg::kSampleNT / 32) * tg::kStreamRing * 20;
+  // the threshold kernel ahead of the stream: opt-in (TG_THETA_FIRST=1).  It
+  // shortens the stream by 13 us on config 4 but costs 17-20 us itself.
+  const char* thenv = getenv("TG_THETA_FIRST");
+  const bool theta_first = thenv && thenv[0] == '1';
   const int64_t es = dtype == TG_DTYPE_F32 ? 4 : 2;
   for (int32_t r0 = 0; r0 < batch; r0 += R) {
     const int32_t n = batch - r0 < R ? batch - r0 : R;
@@ -383,6 +388,14 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
         tg::sample_list_kernel<1><<<g, tg::kSampleNT, smem, st>>>(c);
       TG_CUDA(cudaGetLastError());
       continue;
+    }
+    if (theta_first) {  // every row's threshold first (one warp per row), then the pure stream
+      c.theta_given = 1;
+      const int tg_grid = (n + tg::kThetaRows - 1) / tg::kThetaRows;
+      if (dtype == TG_DTYPE_F32)
+        tg::theta_kernel<0><<<tg_grid, tg::kThetaNT, 0, st>>>(c);
+      else
+        tg::theta_kernel<1><<<tg_grid, tg::kThetaNT, 0, st>>>(c);
     }
     if (dtype == TG_DTYPE_F32)
       tg::sample_kernel<0, true><<<n, tg::kSampleNT, ring_smem, st>>>(c);
