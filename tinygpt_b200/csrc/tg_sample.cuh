@@ -40,9 +40,6 @@ constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold 
 #define TG_UNROLL 4
 #endif
 constexpr int kUnroll = TG_UNROLL;  // 128-bit loads in flight per thread
-#ifndef TG_THETA_PREFETCH
-#define TG_THETA_PREFETCH 8  // 128-bit vectors per thread prefetched to L2 while theta is computed
-#endif
 constexpr int kNoTopkTarget = 512;  // candidate target of rows without top-k
 constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) before the full row
 #ifndef TG_MIN_CTAS
@@ -1509,17 +1506,6 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
         const int j = t + q * NT;
         if (j < nvec) raw[q] = ldg_stream(vrow + j);
       }
-#ifndef TG_NO_THETA_PREFETCH
-      // the streaming kernel computes theta next, with no loads of its own in
-      // flight: keep DRAM busy by pulling the row's next stages into L2
-      if constexpr (kStream) {
-#pragma unroll
-        for (int q = 0; q < TG_THETA_PREFETCH; q++) {
-          const int j = (SV + q) * NT + t;
-          if (j < nvec) asm volatile("prefetch.global.L2 [%0];" ::"l"(vrow + j));
-        }
-      }
-#endif
       // the history hash (counts only) is built while the sample loads fly
       if (!risers) build_hist(0.0f, false);
 #pragma unroll
