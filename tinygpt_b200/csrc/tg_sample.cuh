@@ -1299,22 +1299,25 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
           for (int e = 0; e < EPV; e++) hits |= (((bits >> e) & 1u) && x[e] >= th ? 1u : 0u) << e;
         }
         const int c = __popc(hits);
-        int pre = 0, tot = 0;
+        int incl = c;
 #pragma unroll
-        for (int bit = 0; bit < (EPV >= 8 ? 4 : 3); bit++) {
-          const unsigned m = __ballot_sync(kFull, (c >> bit) & 1);
-          pre += __popc(m & lt) << bit;
-          tot += __popc(m) << bit;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += v;
         }
+        const int tot = __shfl_sync(kFull, incl, 31);
         int base = 0;
-        if (lane == 0 && tot) base = atomicAdd(&sm.cand_count, tot);
-        int pos = __shfl_sync(kFull, base, 0) + pre;
+        if (lane == 31 && tot) base = atomicAdd(&sm.cand_count, tot);
+        int pos = __shfl_sync(kFull, base, 31) + incl - c;
+        // a lane's hits, one set bit at a time (usually one or two of EPV)
+        while (hits) {
+          const int e = __ffs(hits) - 1;
+          hits &= hits - 1u;
+          float xe = x[0];
 #pragma unroll
-        for (int e = 0; e < EPV; e++) {
-          if ((hits >> e) & 1u) {
-            if (pos < kCandMax) { cand_y[pos] = x[e]; cand_id[pos] = head + j * EPV + e; }
-            pos++;
-          }
+          for (int f = 1; f < EPV; f++) xe = e == f ? x[f] : xe;  // register select, no local memory
+          if (pos < kCandMax) { cand_y[pos] = xe; cand_id[pos] = head + j * EPV + e; }
+          pos++;
         }
       }
       __syncwarp();
