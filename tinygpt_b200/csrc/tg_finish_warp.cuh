@@ -32,7 +32,10 @@
 namespace tg {
 
 constexpr int kWfMaxWarps = 16;      // rows per CTA at most
-constexpr int kWfGroupWarps = 28;    // warps per CTA at most (<= 73 registers per thread)
+#ifndef TG_WF_WARPS
+#define TG_WF_WARPS 28
+#endif
+constexpr int kWfGroupWarps = TG_WF_WARPS;  // warps per CTA at most (65536 / (32 x this) registers per thread)
 constexpr int kWfMaxNT = kWfGroupWarps * 32;
 constexpr int kWfSmem = 227 * 1024 - 256;  // dynamic shared memory of a CTA (static: 64 B)
 constexpr int kWfBins = 256;         // histogram bins of one selection round
@@ -123,10 +126,9 @@ __device__ __forceinline__ int sel_shift(K width) {
 
 template <bool kMass, int G>
 __device__ __forceinline__ void sel_zero(const Grp<G>& g, GrpSel& ws) {
-#pragma unroll
-  for (int j = 0; j < kWfBins / (32 * G); j++) {
-    ws.hl[0][g.gt + 32 * G * j] = 0u;
-    if (kMass) { ws.hl[1][g.gt + 32 * G * j] = 0u; ws.hl[2][g.gt + 32 * G * j] = 0u; }
+  for (int i = g.gt; i < kWfBins; i += 32 * G) {
+    ws.hl[0][i] = 0u;
+    if (kMass) { ws.hl[1][i] = 0u; ws.hl[2][i] = 0u; }
   }
 }
 
@@ -534,6 +536,9 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, int 
   // mass total, and the first top-p histogram round over their (s desc, id
   // asc) keys
   const float smax = __fdiv_rn(ymax, T);
+  // every value below kth has a quotient below sk when the next float down does
+  // (__fdiv_rn is monotone in y)
+  const bool below_kth_out = __fdiv_rn(key2f(fkey(kth) - 1u), T) < sk;
   const bool toppon = p.top_p < 1.0f;
   const unsigned long long plo = static_cast<unsigned long long>(~fkey(smax)) << 32;
   const unsigned long long phi = (static_cast<unsigned long long>(~fkey(sk)) << 32) | 0xffffffffull;
@@ -554,7 +559,9 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, int 
     const int id = i < n ? lid[i] : -1;
     __syncwarp();  // writes go only to this warp's slots at or below those loaded
     float sv = 0.0f;
-    bool keep = y >= theta && y > neg_inf();
+    // y >= kth keeps (division is monotone); below kth only a value whose
+    // quotient can still round up to sk needs the division
+    bool keep = y >= theta && y > neg_inf() && (y >= kth || !below_kth_out);
     if (keep) {
       sv = __fdiv_rn(y, T);
       keep = sv >= sk;

@@ -214,7 +214,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   unsigned long long Z = 0;
   if (ok) {
     for (int i = t; i < c1 - c0; i += kSpecNT)
-      Z += qmass(__fsub_rn(__fdiv_rn(elem(i), T), smax));
+      Z += qmass_le0(__fsub_rn(__fdiv_rn(elem(i), T), smax));
   }
   Z = block_sum<kSpecNT>(Z, sm);
   if (t == 0) c_z = Z;
@@ -266,8 +266,8 @@ __device__ __forceinline__ void spec_accept_step(const SpecArgs& a, int b, int i
   } else if (tok >= 0 && tok < V) {
     const char* trow = reinterpret_cast<const char*>(a.target) + (static_cast<int64_t>(b) * (K + 1) + i) * V * E::kSize;
     const char* drow = reinterpret_cast<const char*>(a.draft) + (static_cast<int64_t>(b) * K + i) * V * E::kSize;
-    const unsigned long long qT = qmass(__fsub_rn(__fdiv_rn(E::load(trow, tok), T), st[i].smax));
-    const unsigned long long qD = qmass(__fsub_rn(__fdiv_rn(E::load(drow, tok), T), st[K + 1 + i].smax));
+    const unsigned long long qT = qmass_le0(__fsub_rn(__fdiv_rn(E::load(trow, tok), T), st[i].smax));
+    const unsigned long long qD = qmass_le0(__fsub_rn(__fdiv_rn(E::load(drow, tok), T), st[K + 1 + i].smax));
     const double pT = __ddiv_rn(__ull2double_rn(qT), __ull2double_rn(st[i].Z));
     const double pD = __ddiv_rn(__ull2double_rn(qD), __ull2double_rn(st[K + 1 + i].Z));
     const double ratio = __ddiv_rn(pT, pD > 1e-10 ? pD : 1e-10);
@@ -360,16 +360,17 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const int v0 = min(c1, c0 + t * sub), v1 = min(c1, v0 + sub);
   const uint32_t* msk = !kMask ? nullptr : spec_mask(a, b, pos);
   auto ld = [&](const char* row, int v) { return (msk && !mask_allows(msk, v)) ? neg_inf() : E::load(row, v); };
-  auto qt_of = [&](int v) { return qmass(__fsub_rn(__fdiv_rn(ld(trow, v), T), smT)); };
+  // every d = x / T - max(x / T) <= 0: the branch-free exact mass applies
+  auto qt_of = [&](int v) { return qmass_le0(__fsub_rn(__fdiv_rn(ld(trow, v), T), smT)); };
   auto rq_of = [&](int v) {
-    const unsigned long long qd = qmass(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
+    const unsigned long long qd = qmass_le0(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
     return resid_mass(qt_of(v), ZT, qd, ZD);
   };
   unsigned long long sT = 0, sR = 0;
   if (fin >= 0) {
     for (int v = v0; v < v1; v++) {
       const unsigned long long qt = qt_of(v);
-      const unsigned long long qd = qmass(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
+      const unsigned long long qd = qmass_le0(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
       sT += qt;
       sR += resid_mass(qt, ZT, qd, ZD);
     }

@@ -201,6 +201,8 @@ int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch, tg_s
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tg::finish_warp_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
     if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(tg::finish_warp_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kWfSmem);
+    if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tg::sample_fused_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kFuSmem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(tg::sample_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, tg::kFuSmem);
@@ -408,12 +410,14 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
       // kernel's register count) and 16 warps per row group in all
       int rpc = (n + nsm - 1) / nsm;
       rpc = rpc < 1 ? 1 : (rpc > tg::kWfMaxWarps ? tg::kWfMaxWarps : rpc);
-      const int G = rpc * 4 <= tg::kWfGroupWarps ? 4 : (rpc * 2 <= tg::kWfGroupWarps ? 2 : 1);
+      const int G = rpc * 4 <= tg::kWfGroupWarps ? 4 : rpc * 3 <= tg::kWfGroupWarps ? 3 : (rpc * 2 <= tg::kWfGroupWarps ? 2 : 1);
       const size_t wsb = static_cast<size_t>(rpc) * tg::grp_fin_bytes(a.ht_log2);
       const int pool = static_cast<int>((static_cast<size_t>(tg::kWfSmem) - wsb) / 8);
       const int grid = (n + rpc - 1) / rpc;
       if (G == 4)
         tg::finish_warp_kernel<4><<<grid, rpc * 128, tg::kWfSmem, st>>>(c, pool);
+      else if (G == 3)
+        tg::finish_warp_kernel<3><<<grid, rpc * 96, tg::kWfSmem, st>>>(c, pool);
       else if (G == 2)
         tg::finish_warp_kernel<2><<<grid, rpc * 64, tg::kWfSmem, st>>>(c, pool);
       else
