@@ -1538,17 +1538,33 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
       // (a 4x deeper rank of the sample, the row re-read while it is likely
       // still in L2), where the retry overlaps the other rows' streams, rather
       // than leaving the row to a lone fallback CTA after the finisher.
-      for (int attempt = 0; attempt < kRetries && sm.cand_count < static_cast<int>(need) && theta > neg_inf();
-           attempt++) {
-        rk = rk * 4u;
-        float vm[SV];
+      // A list that overflowed raises theta to the tgt-th largest value it
+      // buffered (every element at or above it is then in the row, so the new
+      // list holds at least tgt >= k), as the fallback would, but here.
+      for (int attempt = 0; attempt < kRetries && theta > neg_inf(); attempt++) {
+        const bool shorted = sm.cand_count < static_cast<int>(need);
+        if (!shorted && sm.cand_count <= kCandMax) break;
+        float nt;
+        if (shorted) {
+          rk = rk * 4u;
+          float vm[SV];
 #pragma unroll
-        for (int q = 0; q < SV; q++) {
-          const int j = t + q * NT;
-          vm[q] = j < nvec ? vmax_of(__ldg(vrow + j), j) : neg_inf();
+          for (int q = 0; q < SV; q++) {
+            const int j = t + q * NT;
+            vm[q] = j < nvec ? vmax_of(__ldg(vrow + j), j) : neg_inf();
+          }
+          nt = sample_theta<SV, NT>(vm, rk, sm);
+          if (!(nt < theta)) nt = neg_inf();
+        } else {
+          uint32_t tk; unsigned long long b0, m0; unsigned int c0, n0;
+          const unsigned int tr = static_cast<unsigned int>(tgt);
+          radix_find<NT, true, false>(
+              SmemSrcT<NT>{cand_y, cand_id, kCandMax, theta}, 32,
+              [&](int, float y, uint32_t& key, unsigned long long& w) { key = fkey(y); w = 0; return true; },
+              [&](unsigned long long, unsigned int c) { return c >= tr; }, sm, tk, b0, c0, n0, m0, 16);
+          nt = key2f(tk);
+          if (!(nt > theta)) break;  // ties all the way up: the fallback's full-row path decides
         }
-        float nt = sample_theta<SV, NT>(vm, rk, sm);
-        if (!(nt < theta)) nt = neg_inf();
         theta = nt;
         if (t == 0) sm.cand_count = 0;
         __syncthreads();
