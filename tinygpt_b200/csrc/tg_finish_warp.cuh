@@ -689,6 +689,9 @@ __device__ bool grp_finish_row(const Grp<G>& g, const SampleArgs& a, int b, int 
 // the fallback list).  Rows a group does not finish go to the fallback list.
 template <int G>
 __global__ void __launch_bounds__(kWfMaxNT, 1) finish_warp_kernel(SampleArgs a, int pool_entries) {
+  // launched as a programmatic dependent of the streaming kernel: its lists are
+  // complete and visible once this returns (a no-op for an ordinary launch)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ int needs[kWfMaxWarps];
   const int R = blockDim.x / (32 * G);  // rows of this CTA

@@ -1733,6 +1733,7 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
 // much and made rows without top-k 1.4-1.7x slower.)
 template <int DT>
 __global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_list_kernel(SampleArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the finisher's list (programmatic launch)
   if (static_cast<int>(blockIdx.x) >= *a.fb_count) return;
   sample_row<DT, false, kSampleNT>(a, a.fb_rows[blockIdx.x]);
 }

@@ -133,6 +133,25 @@ bool getenv_off(const char* name) {
   return v && v[0] == '0';
 }
 
+// Launches `kernel` on `st` as a programmatic dependent of the previous work on
+// the stream: its launch is processed while that work drains, and the kernel
+// waits on the device (griddepcontrol.wait) before it reads anything.
+template <class... KArgs, class... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t st,
+                             Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Rows per streaming / finishing launch pair (bounds the candidate buffer:
 // kCandMax * 8 + 8 bytes per row).
 constexpr int kSplitRows = 4096;
@@ -414,19 +433,22 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
       const size_t wsb = static_cast<size_t>(rpc) * tg::grp_fin_bytes(a.ht_log2);
       const int pool = static_cast<int>((static_cast<size_t>(tg::kWfSmem) - wsb) / 8);
       const int grid = (n + rpc - 1) / rpc;
+      cudaError_t le;
       if (G == 4)
-        tg::finish_warp_kernel<4><<<grid, rpc * 128, tg::kWfSmem, st>>>(c, pool);
+        le = launch_dependent(tg::finish_warp_kernel<4>, grid, rpc * 128, tg::kWfSmem, st, c, pool);
       else if (G == 3)
-        tg::finish_warp_kernel<3><<<grid, rpc * 96, tg::kWfSmem, st>>>(c, pool);
+        le = launch_dependent(tg::finish_warp_kernel<3>, grid, rpc * 96, tg::kWfSmem, st, c, pool);
       else if (G == 2)
-        tg::finish_warp_kernel<2><<<grid, rpc * 64, tg::kWfSmem, st>>>(c, pool);
+        le = launch_dependent(tg::finish_warp_kernel<2>, grid, rpc * 64, tg::kWfSmem, st, c, pool);
       else
-        tg::finish_warp_kernel<1><<<grid, rpc * 32, tg::kWfSmem, st>>>(c, pool);
+        le = launch_dependent(tg::finish_warp_kernel<1>, grid, rpc * 32, tg::kWfSmem, st, c, pool);
+      TG_CUDA(le);
       const int g = n;  // one CTA per possible fallback row
       if (dtype == TG_DTYPE_F32)
-        tg::sample_list_kernel<0><<<g, tg::kSampleNT, smem, st>>>(c);
+        le = launch_dependent(tg::sample_list_kernel<0>, g, tg::kSampleNT, smem, st, c);
       else
-        tg::sample_list_kernel<1><<<g, tg::kSampleNT, smem, st>>>(c);
+        le = launch_dependent(tg::sample_list_kernel<1>, g, tg::kSampleNT, smem, st, c);
+      TG_CUDA(le);
     } else if (dtype == TG_DTYPE_F32) {
       tg::sample_kernel<0><<<n, tg::kSampleNT, smem, st>>>(c);
     } else {
