@@ -1721,7 +1721,12 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
 
 template <int DT, bool kStream = false, int NT = kSampleNT>
 __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerSm * kSampleNT / NT > 0 ? kMinCtasPerSm * kSampleNT / NT : 1)) sample_kernel(SampleArgs a) {
-  if constexpr (kStream) {  // the fallback list of this launch pair starts empty
+  if constexpr (kStream) {
+    // launched as a programmatic dependent of whatever ran before on the stream
+    // (the previous call's fallback kernel still reads the candidate buffer
+    // this kernel overwrites; a producer kernel writes the logits)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the fallback list of this launch pair starts empty
     if (a.fb_count && blockIdx.x == 0 && threadIdx.x == 0) *a.fb_count = 0;
   }
   sample_row<DT, kStream, NT>(a, blockIdx.x);

@@ -418,10 +418,9 @@ static int32_t launch_sample(tg_sampler* s, int32_t vocab_offset, int32_t full_v
       else
         tg::theta_kernel<1><<<tg_grid, tg::kThetaNT, 0, st>>>(c);
     }
-    if (dtype == TG_DTYPE_F32)
-      tg::sample_kernel<0, true><<<n, tg::kSampleNT, ring_smem, st>>>(c);
-    else
-      tg::sample_kernel<1, true><<<n, tg::kSampleNT, ring_smem, st>>>(c);
+    TG_CUDA(dtype == TG_DTYPE_F32
+                ? launch_dependent(tg::sample_kernel<0, true>, n, tg::kSampleNT, ring_smem, st, c)
+                : launch_dependent(tg::sample_kernel<1, true>, n, tg::kSampleNT, ring_smem, st, c));
     if (mark) TG_CUDA(cudaEventRecord(s->prof_ev[1], st));
     if (warp_fin) {  // a warp per row, then the rows it left on CTAs
       // one CTA per SM with ceil(n / SMs) rows; G warps per row, G the largest
