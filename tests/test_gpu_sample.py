@@ -271,3 +271,17 @@ def test_config4_batch_8192(oracle_mod, sampler_factory):
     w = W.make(4, seed=7, batch=8192)
     s = sampler_factory(w["vocab"], max_batch=8192)
     assert_same(oracle_mod, s, w, what="config 4 B=8192")
+
+
+@pytest.mark.parametrize("make", ["sorted", "ties", "penalties", "masks"])
+def test_edge_workloads_two_kernel_mode(oracle_mod, sampler_factory, make):
+    """The edge workloads at 1100 rows: the two-kernel mode (streaming kernel
+    with its in-kernel threshold retries, warp-group finisher, fallback kernel
+    for the rows the finisher leaves)."""
+    w = {"sorted": _sorted_w, "ties": _ties_w, "penalties": _pen_w, "masks": _masks_w}[make]()
+    V = w["logits"].shape[1]
+    s = sampler_factory(V)
+    s.path_counters()
+    assert_same(oracle_mod, s, _tile(w, 1100), what=f"{make} x1100 two-kernel")
+    c = s.path_counters()
+    assert c["candidate"] + c["full_row"] >= 1100
