@@ -316,7 +316,9 @@ int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits);
  *   [2] rows with fewer than k candidates         -> full-row path
  *   [3] rows whose top-k threshold fell below the candidate bound -> full-row path
  *   [4] rows processed by the full-row path (any reason)
- *   [5] candidates appended (sum over rows)
+ *   [5] candidates appended (sum over rows; single-kernel mode)
+ *   [6] rows of [0] finished by the warp-group finisher (calls of >= 1024 rows)
+ *   [7] rows the warp-group finisher left because its shared-memory pool was full
  * Copies min(n, TG_PATH_COUNTERS) counters (synchronizes the device); zeroes
  * them when reset != 0. */
 #define TG_PATH_COUNTERS 8

@@ -265,7 +265,8 @@ class Sampler:
         """Row counts per sampling path since the last reset (see tgsample.h)."""
         buf = (ctypes.c_uint64 * 8)()
         check(self._L.tg_sampler_path_counters(self._h, buf, 8, int(reset)))
-        keys = ["candidate", "overflow", "short", "threshold", "full_row", "candidates"]
+        keys = ["candidate", "overflow", "short", "threshold", "full_row", "candidates", "warp_finished",
+                "pool_full"]
         return {k: int(buf[i]) for i, k in enumerate(keys)}
 
     def profile(self, enable: bool = True):
