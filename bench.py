@@ -191,7 +191,7 @@ def run_reference(args, rank, world):
 def run_config(args):
     """One JSON line for one of the five workloads (`--config N`, one GPU): the
     device time of a tg_sample / tg_spec_verify call on resident inputs, CUDA
-    events over `--steps` calls (config 1: calls replayed from a CUDA graph, the
+    events over `--steps` calls (configs 1 and 2: calls replayed from a CUDA graph, the
     latency of one call).  Inputs come from tinygpt_b200.workloads (the
     oracle-checked workloads); configs 3-5 exceed L2 (two sets alternate for 3
     and 4; config 5 is 722 MB per call), configs 1-2 are L2-resident."""
@@ -246,7 +246,15 @@ def run_config(args):
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if cfg == 1:  # latency: a graph of G calls, replayed
+    loop_us = None
+    if cfg == 2:  # the same calls issued from the host one by one (bound by the host loop)
+        e0.record(stream)
+        for i in range(args.steps):
+            call(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        loop_us = e0.elapsed_time(e1) * 1e3 / args.steps
+    if cfg in (1, 2):  # latency-bound sizes: a graph of G calls, replayed (no host launch gaps)
         G = 100
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
@@ -280,10 +288,12 @@ def run_config(args):
             "config": {"workload": f"config {cfg}", "vocab": Vc, "batch": Bc,
                        "l2": "inputs larger than L2, two sets alternate" if cfg in (3, 4) else
                              ("722 MB per call, larger than L2" if cfg == 5 else "L2-resident (latency-bound size)"),
-                       "timing": "CUDA graph of 100 calls, replayed" if cfg == 1 else "CUDA events over back-to-back calls"},
+                       "timing": "CUDA graph of 100 calls, replayed" if cfg in (1, 2) else "CUDA events over back-to-back calls"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "algorithmic_bytes_per_call": bytes_call,
                          "peak_source": peak_kind}}
+    if loop_us is not None:
+        line["host_loop_us_per_call"] = loop_us
     if cfg == 3:  # the 64 mask rows are read from L2 after the first touch: count the table once per call
         once = Vc * 4 * Bc + sets[0]["mask_table"].nbytes
         a1 = once / (us * 1e-6) / 1e9

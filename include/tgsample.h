@@ -206,7 +206,7 @@ int32_t tg_spec_verify_masked(tg_sampler* s, const void* target_logits,
  * before any stream capture.  All calls on a device share the array, so calls
  * that overlap on the GPU (different streams without ordering) race.
  * Arguments and results are those of tg_spec_verify, on CUDA device `device`;
- * data errors (bits 1, 3 and 4 of the device status word) are kept in a status
+ * data errors (bits 1 and 4 of the device status word) are kept in a status
  * word inside the same array, cleared at the start of every call and read by
  * tg_spec_verify_static_status. */
 #define TG_STATIC_SPEC_MAX_ROWS 8192
@@ -304,7 +304,7 @@ int32_t tg_sampler_set_collective_timeout(tg_sampler* s, int32_t timeout_ms);
  * bit 1: a draft id outside [0, vocab); bit 2: a row the vocab-sharded mode
  * could not resolve (unsupported parameters, more than TG_SHARD_CAP local
  * survivors, or a top-k threshold tie between shards); bit 3: a bounded wait
- * for a bulk copy into shared memory gave up (the affected statistics are
+ * of the opt-in fused sampling kernel (TG_FUSED=1) gave up (its rows are
  * unreliable); bit 4: a stochastic row in a verification called without
  * draft logits (it ends without a token).  Cleared by this call. */
 int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits);

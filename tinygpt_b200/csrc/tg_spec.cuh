@@ -5,11 +5,11 @@
 // K positions on the host with two softmaxes and several device->host reads per
 // position; here two cluster kernels do the whole batch:
 //   spec_stats_kernel   one 8-CTA cluster per (row, position, target|draft) vocab
-//                       row.  Each CTA stages its slice of the row in shared
-//                       memory with one 1-D TMA bulk copy (cp.async.bulk, no
-//                       multicast), the row maximum and the exact mass sum
-//                       Z = sum q are combined over distributed shared memory:
-//                       the row is read from HBM once.
+//                       row.  Each CTA streams its slice of the row from HBM
+//                       once (maximum; lines kept in L2 with an evict_last
+//                       policy) and re-reads it from L2 for the exact mass sum
+//                       Z = sum q; the slice results are combined over
+//                       distributed shared memory.
 //   spec_verify_kernel  one 8-CTA cluster per batch row.  Rank 0 runs the
 //                       sequential accept chain; every CTA sums the final
 //                       distribution's masses over its slice; the slice sums,
@@ -28,8 +28,6 @@ namespace cg = cooperative_groups;
 
 constexpr int kSpecNT = 256;
 constexpr int kSpecCluster = 8;
-constexpr int kSpecMaxStage = 200 * 1024;     // bytes of a staged slice
-constexpr unsigned kWaitLimit = 1u << 22;     // bounded mbarrier waits
 
 struct __align__(16) SpecStat {
   float smax;
@@ -80,59 +78,78 @@ __device__ __forceinline__ const uint32_t* spec_mask(const SpecArgs& a, int b, i
 
 __device__ __forceinline__ float spec_T(float t0) { return fmaxf(t0, 1e-5f); }
 
-// Bounded wait on phase 0 of an mbarrier; false when the limit ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar) {
-  for (unsigned it = 0; it < kWaitLimit; it++) {
-    uint32_t done;
+// 128-bit load with an L2 eviction policy (createpolicy): the statistics
+// kernel streams its slice from HBM once keeping the lines (evict_last), then
+// re-reads them from L2 for the masses and lets them go (evict_first).
+template <bool kKeep>
+__device__ __forceinline__ uint4 ld_l2hint(const uint4* p) {
+  uint4 v;
+  if constexpr (kKeep) {
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0; selp.u32 %0, 1, 0, p; }"
-        : "=r"(done)
-        : "r"(smem_u32(bar))
-        : "memory");
-    if (done) return true;
+        "{ .reg .b64 pol; createpolicy.fractional.L2::evict_last.b64 pol, 1.0;"
+        " ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], pol; }"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+  } else {
+    asm volatile(
+        "{ .reg .b64 pol; createpolicy.fractional.L2::evict_first.b64 pol, 1.0;"
+        " ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], pol; }"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
   }
-  return false;
+  return v;
 }
 
-// Stage elements [c0, c1) of `row` into shared memory `dst` (raw dtype): the
-// 16-byte-aligned body by one bulk copy completing on `bar`, the rest by plain
-// loads.  Returns whether a bulk copy was issued (then wait on bar).
-template <int DT>
-__device__ __forceinline__ bool stage_slice(const char* row, int c0, int c1, unsigned char* dst,
-                                            uint64_t* bar) {
+constexpr int kSpecLoads = 4;  // 16-byte loads in flight per thread
+
+// Visit elements [0, n) of a slice at `src` (global memory): f(i, x) for each,
+// x = -inf where the mask row `msk` (bit c0 + i) clears it.  A thread visits
+// its elements in increasing index order.  The 16-byte-aligned body goes as
+// kSpecLoads vectors in flight per thread; the rest element by element.
+template <int DT, bool kKeep, class F>
+__device__ __forceinline__ void slice_for_each(const char* src, int n, int c0, const uint32_t* msk, F&& f) {
   using E = Elt<DT>;
-  const int n = c1 - c0;
-  const char* src = row + static_cast<int64_t>(c0) * E::kSize;
-  const bool aligned = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-  const int nb = aligned ? ((n * E::kSize) & ~15) : 0;
-  if (threadIdx.x == 0 && nb > 0) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(nb)
-                 : "memory");
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(nb), "r"(smem_u32(bar))
-        : "memory");
+  constexpr int EPV = E::kEPV;
+  const int t = threadIdx.x;
+  const int nv = (reinterpret_cast<uintptr_t>(src) & 15u) == 0 ? n / EPV : 0;
+  const uint4* sv = reinterpret_cast<const uint4*>(src);
+  for (int j0 = 0; j0 < nv; j0 += kSpecLoads * kSpecNT) {
+    uint4 w[kSpecLoads];
+#pragma unroll
+    for (int q = 0; q < kSpecLoads; q++) {
+      const int j = j0 + q * kSpecNT + t;
+      if (j < nv) w[q] = ld_l2hint<kKeep>(sv + j);
+    }
+#pragma unroll
+    for (int q = 0; q < kSpecLoads; q++) {
+      const int j = j0 + q * kSpecNT + t;
+      if (j >= nv) break;
+      float x[EPV];
+      E::unpack(w[q], x);
+      const uint32_t bits = msk ? mask_bits(msk, c0 + j * EPV, EPV) : 0xffu;
+#pragma unroll
+      for (int e = 0; e < EPV; e++) f(j * EPV + e, ((bits >> e) & 1u) ? x[e] : neg_inf());
+    }
   }
-  for (int i = nb / E::kSize + threadIdx.x; i < n; i += kSpecNT) {
-    if (E::kSize == 4) reinterpret_cast<float*>(dst)[i] = E::load(src, i);
-    else reinterpret_cast<uint16_t*>(dst)[i] = reinterpret_cast<const uint16_t*>(src)[i];
+  for (int i = nv * EPV + t; i < n; i += kSpecNT) {
+    const float x = E::load(src, i);
+    f(i, (msk && !mask_allows(msk, c0 + i)) ? neg_inf() : x);
   }
-  return nb > 0;
 }
 
-template <int DT>
-__device__ __forceinline__ float smem_elem(const unsigned char* buf, int i) {
-  if (Elt<DT>::kSize == 4) return reinterpret_cast<const float*>(buf)[i];
-  return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(buf)[i]) << 16);
-}
-
+// Statistics of one vocab row on an 8-CTA cluster, each CTA one slice.  Pass 1
+// streams the slice from HBM (maximum, first argmax); the cluster combines the
+// slice maxima over distributed shared memory; pass 2 re-reads the slice from
+// L2 for the exact mass sum Z.  No shared-memory staging: occupancy is set by
+// registers, so CTAs of different rows overlap their HBM streams with other
+// CTAs' mass arithmetic.
 template <int DT, bool kMask>
-__global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
+__global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT, 4)
     spec_stats_kernel(SpecArgs a) {
   using E = Elt<DT>;
-  extern __shared__ __align__(128) unsigned char slice[];
-  __shared__ __align__(8) uint64_t bar;
+  // launched as a programmatic dependent: the previous launch of the chain
+  // (statistics, accept tests) must be complete before anything is read
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ ReduceScratch sm;
   __shared__ float c_max;
   __shared__ int c_arg;
@@ -169,30 +186,16 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     row = reinterpret_cast<const char*>(a.draft) + (static_cast<int64_t>(b) * a.K + (pos - a.K - 1)) * V * E::kSize;
   }
   const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
+  const char* src = row + static_cast<int64_t>(c0) * E::kSize;
   const uint32_t* msk = !kMask ? nullptr : spec_mask(a, b, pos <= a.K ? pos : pos - a.K - 1);
-  // element i of the slice, -inf where the position's mask clears it
-  auto elem = [&](int i) {
-    const float x = smem_elem<DT>(slice, i);
-    return (msk && !mask_allows(msk, c0 + i)) ? neg_inf() : x;
-  };
-  if (t == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bar)) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  const bool bulk = stage_slice<DT>(row, c0, c1, slice, &bar);
-  bool ok = true;
-  if (bulk) ok = mbar_wait(&bar);
-  __syncthreads();
-  // pass 1: maximum and its first index
+  // pass 1: maximum and its first index (`x > y` keeps the first)
   float y = neg_inf();
   int id = 0x7fffffff;
-  if (ok) {
-    for (int i = t; i < c1 - c0; i += kSpecNT) {
-      const float x = elem(i);
-      if (x > y) { y = x; id = c0 + i; }
-    }
-  }
+  auto amax = [&](int i, float x) {
+    if (x > y) { y = x; id = c0 + i; }
+  };
+  if (greedy) slice_for_each<DT, false>(src, c1 - c0, c0, msk, amax);  // read once: no need to keep
+  else slice_for_each<DT, true>(src, c1 - c0, c0, msk, amax);
   block_argmax<kSpecNT>(y, id, sm);
   if (t == 0) { c_max = y; c_arg = id; }
   cluster.sync();
@@ -204,18 +207,16 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   if (msk && id == 0x7fffffff) id = -1;  // nothing allowed above -inf
   if (greedy) {
     if (rank == 0 && t == 0) a.stats[r] = SpecStat{y, id, 0ull};
-    if (!ok && t == 0) atomicOr(a.status, 8u);
     cluster.sync();  // peers still read this CTA's maximum
-    if (!ok && bulk) mbar_wait(&bar);  // the copy that gave up must not land after the CTA exits
     return;
   }
   const float T = spec_T(t0);
   const float smax = __fdiv_rn(y, T);
+  // pass 2: the exact masses (d = x / T - smax <= 0: the branch-free form)
   unsigned long long Z = 0;
-  if (ok) {
-    for (int i = t; i < c1 - c0; i += kSpecNT)
-      Z += qmass_le0(__fsub_rn(__fdiv_rn(elem(i), T), smax));
-  }
+  slice_for_each<DT, false>(src, c1 - c0, c0, msk, [&](int, float x) {
+    Z += qmass_le0(__fsub_rn(__fdiv_rn(x, T), smax));
+  });
   Z = block_sum<kSpecNT>(Z, sm);
   if (t == 0) c_z = Z;
   cluster.sync();
@@ -224,9 +225,7 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     for (int q = 0; q < kSpecCluster; q++) tot += *cluster.map_shared_rank(&c_z, q);
     a.stats[r] = SpecStat{smax, id, tot};
   }
-  if (!ok && t == 0) atomicOr(a.status, 8u);
-  cluster.sync();
-  if (!ok && bulk) mbar_wait(&bar);  // never leave with the copy in flight if it can be helped
+  cluster.sync();  // peers still read this CTA's sum
 }
 
 // Residual mass of one token: trunc(max(0, qT/ZT - qD/ZD) * 2^52).
@@ -234,6 +233,19 @@ __device__ __forceinline__ unsigned long long resid_mass(unsigned long long qT, 
                                                          unsigned long long qD, double ZD) {
   const double d = __dsub_rn(__ddiv_rn(__ull2double_rn(qT), ZT), __ddiv_rn(__ull2double_rn(qD), ZD));
   return d > 0.0 ? __double2ull_rz(__dmul_rn(d, kResidScale)) : 0ull;
+}
+
+// resid_mass with an exact early-out: when qT / ZT <= qD / ZD as real numbers
+// (qT * ZD <= qD * ZT in 128-bit integers; ZT and ZD hold integer values, ZTi
+// and ZDi are the same integers), the rounded quotients keep that order, the
+// difference is <= 0 and the residual is 0 -- the divisions are skipped.
+__device__ __forceinline__ unsigned long long resid_mass_x(unsigned long long qT, double ZT,
+                                                           unsigned long long ZTi, unsigned long long qD,
+                                                           double ZD, unsigned long long ZDi) {
+  const unsigned long long h1 = __umul64hi(qT, ZDi), l1 = qT * ZDi;
+  const unsigned long long h2 = __umul64hi(qD, ZTi), l2 = qD * ZTi;
+  if (h1 < h2 || (h1 == h2 && l1 <= l2)) return 0ull;
+  return resid_mass(qT, ZT, qD, ZD);
 }
 
 // One accept test of batch row b at position i (thread-level): appends to out
@@ -283,6 +295,7 @@ __device__ __forceinline__ void spec_accept_step(const SpecArgs& a, int b, int i
 // Lazy mode: position i of every row still accepting, one thread per row.
 template <int DT, bool kMask>
 __global__ void __launch_bounds__(128) spec_chain_kernel(SpecArgs a, int i) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the statistics of position i
   const int b = blockIdx.x * 128 + threadIdx.x;
   if (b >= a.batch) return;
   int32_t* out = a.out_ids + static_cast<int64_t>(b) * (a.K + 1);
@@ -303,6 +316,7 @@ template <int DT, bool kMask>
 __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     spec_verify_kernel(SpecArgs a) {
   using E = Elt<DT>;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the last statistics / accept launch
   __shared__ ReduceScratch sm;
   __shared__ int s_fin, s_n;  // rank 0: the rejecting position (-1 bonus, -2 done) and accepted count
   __shared__ unsigned long long c_sumT, c_sumR;
@@ -355,8 +369,11 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const double ZT = __ull2double_rn(st[pos].Z);
   const float smD = fin < 0 ? 0.0f : st[K + 1 + fin].smax;
   const double ZD = fin < 0 ? 1.0 : __ull2double_rn(st[K + 1 + fin].Z);
+  const unsigned long long ZTi = __double2ull_rn(ZT), ZDi = __double2ull_rn(ZD);  // exact: integer values
+  constexpr int EPV = E::kEPV;
   const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
-  const int sub = (c1 - c0 + kSpecNT - 1) / kSpecNT;
+  // a whole number of 16-byte vectors per thread (c0 is a multiple of 8)
+  const int sub = ((c1 - c0 + kSpecNT - 1) / kSpecNT + EPV - 1) / EPV * EPV;
   const int v0 = min(c1, c0 + t * sub), v1 = min(c1, v0 + sub);
   const uint32_t* msk = !kMask ? nullptr : spec_mask(a, b, pos);
   auto ld = [&](const char* row, int v) { return (msk && !mask_allows(msk, v)) ? neg_inf() : E::load(row, v); };
@@ -364,18 +381,47 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   auto qt_of = [&](int v) { return qmass_le0(__fsub_rn(__fdiv_rn(ld(trow, v), T), smT)); };
   auto rq_of = [&](int v) {
     const unsigned long long qd = qmass_le0(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
-    return resid_mass(qt_of(v), ZT, qd, ZD);
+    return resid_mass_x(qt_of(v), ZT, ZTi, qd, ZD, ZDi);
   };
   unsigned long long sT = 0, sR = 0;
+  int vs = v0;  // first element of the scalar rest
+  // unmasked rows on 16-byte boundaries: the thread's run as vectors (the run is
+  // contiguous, so the lines a load misses are the next loads' L1 hits)
+  const bool vec = !kMask && v1 > v0 &&
+                   ((reinterpret_cast<uintptr_t>(trow) | reinterpret_cast<uintptr_t>(drow)) & 15u) == 0;
+  if (vec) {
+    const int nvv = (v1 - v0) / EPV;
+    const uint4* tv = reinterpret_cast<const uint4*>(trow + static_cast<int64_t>(v0) * E::kSize);
+    const uint4* dv = fin >= 0 ? reinterpret_cast<const uint4*>(drow + static_cast<int64_t>(v0) * E::kSize) : nullptr;
+    for (int j = 0; j < nvv; j++) {
+      float xt[EPV];
+      E::unpack(__ldg(tv + j), xt);
+      if (fin >= 0) {
+        float xd[EPV];
+        E::unpack(__ldg(dv + j), xd);
+#pragma unroll
+        for (int e = 0; e < EPV; e++) {
+          const unsigned long long qt = qmass_le0(__fsub_rn(__fdiv_rn(xt[e], T), smT));
+          const unsigned long long qd = qmass_le0(__fsub_rn(__fdiv_rn(xd[e], T), smD));
+          sT += qt;
+          sR += resid_mass_x(qt, ZT, ZTi, qd, ZD, ZDi);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPV; e++) sT += qmass_le0(__fsub_rn(__fdiv_rn(xt[e], T), smT));
+      }
+    }
+    vs = v0 + nvv * EPV;
+  }
   if (fin >= 0) {
-    for (int v = v0; v < v1; v++) {
+    for (int v = vs; v < v1; v++) {
       const unsigned long long qt = qt_of(v);
       const unsigned long long qd = qmass_le0(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
       sT += qt;
-      sR += resid_mass(qt, ZT, qd, ZD);
+      sR += resid_mass_x(qt, ZT, ZTi, qd, ZD, ZDi);
     }
   } else {
-    for (int v = v0; v < v1; v++) sT += qt_of(v);
+    for (int v = vs; v < v1; v++) sT += qt_of(v);
   }
   unsigned long long ctaT, ctaR;
   const unsigned long long befT = block_excl_scan<kSpecNT>(sT, ctaT, sm);
@@ -409,6 +455,26 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   cluster.sync();  // keep this CTA's shared memory alive for its peers
 }
 
+// Launch on `st` as a programmatic dependent of the previous work on the
+// stream (every spec kernel starts with griddepcontrol.wait), so each launch of
+// the chain is set up while the previous one drains.  The cluster shape comes
+// from the kernels' __cluster_dims__.
+template <class... KArgs, class... Args>
+inline cudaError_t spec_launch(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t st,
+                               Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // One verification on `st`.  Eager: statistics of every position, then the
 // chain and the draw (two launches).  Lazy (rstate given): statistics of
 // position i only for the rows still accepting, i = 0..K-1, each followed by
@@ -416,30 +482,27 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
 // then the draw (2K + 2 launches, fewer vocab rows read).
 template <int DT, bool kMask>
 inline cudaError_t launch_spec_t(SpecArgs a, cudaStream_t st) {
-  const int esz = Elt<DT>::kSize;
   int chunk = (a.vocab + kSpecCluster - 1) / kSpecCluster;
   chunk = (chunk + 7) / 8 * 8;
   a.chunk = chunk;
-  const size_t stage = static_cast<size_t>(chunk) * esz;
-  if (stage > static_cast<size_t>(kSpecMaxStage)) return cudaErrorInvalidValue;
-  if (stage > 48 * 1024) {  // per device; cheap enough to repeat
-    cudaError_t e = cudaFuncSetAttribute(spec_stats_kernel<DT, kMask>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSpecMaxStage);
-    if (e != cudaSuccess) return e;
-  }
+  const size_t stage = 0;  // no dynamic shared memory
+  cudaError_t e = cudaSuccess;
   if (!a.rstate) {
     const int nrows = a.batch * (2 * a.K + 1);
-    spec_stats_kernel<DT, kMask><<<nrows * kSpecCluster, kSpecNT, stage, st>>>(a);
+    e = spec_launch(spec_stats_kernel<DT, kMask>, nrows * kSpecCluster, kSpecNT, stage, st, a);
   } else {
-    for (int i = 0; i < a.K; i++) {
+    for (int i = 0; i < a.K && e == cudaSuccess; i++) {
       a.lazy_pos = i;
-      spec_stats_kernel<DT, kMask><<<a.batch * 2 * kSpecCluster, kSpecNT, stage, st>>>(a);
-      spec_chain_kernel<DT, kMask><<<(a.batch + 127) / 128, 128, 0, st>>>(a, i);
+      e = spec_launch(spec_stats_kernel<DT, kMask>, a.batch * 2 * kSpecCluster, kSpecNT, stage, st, a);
+      if (e == cudaSuccess)
+        e = spec_launch(spec_chain_kernel<DT, kMask>, (a.batch + 127) / 128, 128, 0, st, a, i);
     }
     a.lazy_pos = a.K;
-    spec_stats_kernel<DT, kMask><<<a.batch * kSpecCluster, kSpecNT, stage, st>>>(a);
+    if (e == cudaSuccess)
+      e = spec_launch(spec_stats_kernel<DT, kMask>, a.batch * kSpecCluster, kSpecNT, stage, st, a);
   }
-  spec_verify_kernel<DT, kMask><<<a.batch * kSpecCluster, kSpecNT, 0, st>>>(a);
+  if (e == cudaSuccess) e = spec_launch(spec_verify_kernel<DT, kMask>, a.batch * kSpecCluster, kSpecNT, 0, st, a);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
