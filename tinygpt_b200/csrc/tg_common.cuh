@@ -63,6 +63,20 @@ __device__ __forceinline__ uint64_t qmass_le0(float d) {
   return d >= -32.0f ? q : 0ull;
 }
 
+// Hash of a token id for the history tables: the 32-bit finaliser of
+// MurmurHash3 (fmix32), so every id bit reaches every hash bit.  A plain
+// multiplicative hash maps ids in arithmetic progression (an affine token
+// permutation, a tokenizer's id blocks) onto runs of neighbouring slots, and
+// linear probing then walks those runs on every lookup.
+__device__ __forceinline__ uint32_t tg_mix32(uint32_t h) {
+  h ^= h >> 16;
+  h *= 0x85EBCA6Bu;
+  h ^= h >> 13;
+  h *= 0xC2B2AE35u;
+  h ^= h >> 16;
+  return h;
+}
+
 // Order-preserving 32-bit key of a float (-0 folded onto +0).
 __device__ __forceinline__ uint32_t fkey(float x) {
   const uint32_t u = __float_as_uint(x == 0.0f ? 0.0f : x);

@@ -290,11 +290,13 @@ __device__ bool grp_select(const Grp<G>& g, Iter iter, Wt wt, K lo, K hi, bool p
 
 // History hash slot: ((id + 1) << 11) | count; 0 = empty.  Counts stay below
 // 2^11 because histories served here hold at most kWfMaxHist ids.
+// Slot from the low bits of the mixed id hash (tg_mix32), Bloom bit from its
+// high 13 bits.
 __device__ __forceinline__ int wf_slot0(int id, int mask) {
-  return static_cast<int>((static_cast<uint32_t>(id) * 0x9E3779B1u) >> 12) & mask;
+  return static_cast<int>(tg_mix32(static_cast<uint32_t>(id))) & mask;
 }
 __device__ __forceinline__ uint32_t wf_bloom_bit(int id) {
-  return (static_cast<uint32_t>(id) * 0x85EBCA77u) >> 19;  // 13 bits
+  return tg_mix32(static_cast<uint32_t>(id)) >> 19;  // 13 bits
 }
 
 // Diagnostic build only (-DTG_PHASE_TIMING): cycles per stage of the warp

@@ -77,14 +77,20 @@ static_assert(kCandMax <= kWideMassN, "candidate mass histograms must not overfl
 // Diagnostic build only (-DTG_PHASE_TIMING): cycles per phase summed over CTAs.
 #ifdef TG_PHASE_TIMING
 __device__ unsigned long long g_phase_cycles[32];
+// cycles per phase of rows 0..255 (16 phases each), summed over calls
+__device__ unsigned long long g_row_phase[256 * 16];
 #endif
 struct PhaseClock {
   long long last = 0;
+  int row = -1;
   __device__ __forceinline__ void mark(int i) {
 #ifdef TG_PHASE_TIMING
     if (threadIdx.x == 0) {
       const long long now = clock64();
-      if (last) atomicAdd(&g_phase_cycles[i], static_cast<unsigned long long>(now - last));
+      if (last) {
+        atomicAdd(&g_phase_cycles[i], static_cast<unsigned long long>(now - last));
+        if (row >= 0 && row < 256 && i < 16) atomicAdd(&g_row_phase[row * 16 + i], static_cast<unsigned long long>(now - last));
+      }
       last = now;
     }
 #else
@@ -142,12 +148,15 @@ struct Hist {
   int mask;
   int log2;
   int active;
+  // Bloom bit (12 bits) from the low bits of the same mixed hash, the slot
+  // from its high bits
+  __device__ __forceinline__ static uint32_t bloom_bit(int id) { return tg_mix32(static_cast<uint32_t>(id)) & 4095u; }
   __device__ __forceinline__ int slot0(int id) const {
-    return static_cast<int>((static_cast<uint32_t>(id) * 0x9E3779B1u) >> (32 - log2));
+    return static_cast<int>(tg_mix32(static_cast<uint32_t>(id)) >> (32 - log2));  // high bits
   }
   __device__ __forceinline__ bool find(int id, float& y) const {
     if (!active) return false;
-    const uint32_t h = (static_cast<uint32_t>(id) * 0x85EBCA77u) >> 20;
+    const uint32_t h = bloom_bit(id);
     if (!((bloom[h >> 5] >> (h & 31)) & 1u)) return false;
     int s = slot0(id);
     for (;;) {
@@ -1107,6 +1116,7 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
   int* hval = hkey + ht;
 
   PhaseClock pc;
+  pc.row = b;
   pc.mark(0);
   const tg_row_params p = a.params[b];
   const char* row = reinterpret_cast<const char*>(a.logits) + b * a.row_stride * E::kSize;
@@ -1191,7 +1201,7 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
     for (int s = t; s < ht; s += NT) {
       const int id = hkey[s];
       if (id < 0) continue;
-      const uint32_t hb = (static_cast<uint32_t>(id) * 0x85EBCA77u) >> 20;
+      const uint32_t hb = Hist::bloom_bit(id);
       atomicOr(&bloom[hb >> 5], 1u << (hb & 31));
       if (!values) continue;
       float raw = E::load(row, id);

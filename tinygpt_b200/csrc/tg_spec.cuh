@@ -28,6 +28,10 @@ namespace cg = cooperative_groups;
 
 constexpr int kSpecNT = 256;
 constexpr int kSpecCluster = 8;
+#ifndef TG_VERIFY_MINB
+#define TG_VERIFY_MINB 4
+#endif
+constexpr int kVerifyMinCtas = TG_VERIFY_MINB;  // verify kernel occupancy target (registers <= 64)
 
 struct __align__(16) SpecStat {
   float smax;
@@ -313,13 +317,15 @@ __global__ void __launch_bounds__(128) spec_chain_kernel(SpecArgs a, int i) {
 }
 
 template <int DT, bool kMask>
-__global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
+__global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT, kVerifyMinCtas)
     spec_verify_kernel(SpecArgs a) {
   using E = Elt<DT>;
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the last statistics / accept launch
   __shared__ ReduceScratch sm;
   __shared__ int s_fin, s_n;  // rank 0: the rejecting position (-1 bonus, -2 done) and accepted count
   __shared__ unsigned long long c_sumT, c_sumR;
+  __shared__ int s_ent;                  // the table entry holding the draw point
+  __shared__ unsigned long long s_before;  // mass before that entry
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int t = threadIdx.x;
@@ -360,8 +366,12 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
     return;
   }
 
-  // Final draw over the vocab in index order: this CTA's slice [c0, c1),
-  // thread t owning the contiguous part [c0 + t*sub, ...).
+  // Final draw over the vocab in index order.  The CTA's slice [c0, c1) is cut
+  // into tiles of kSpecNT * EPV elements; thread t takes the EPV consecutive
+  // elements [tile * TE + t * EPV, ...) of every tile (coalesced 16-byte loads).
+  // Each warp's sums per tile go to a shared table, in index order, so the
+  // draw point's (tile, warp) is found by a scan of the table and that warp
+  // alone re-reads its 32 * EPV elements to place it.
   const int pos = fin < 0 ? K : fin;
   const char* trow = tgt + static_cast<int64_t>(pos) * V * E::kSize;
   const char* drow = fin < 0 ? nullptr : drf + static_cast<int64_t>(fin) * V * E::kSize;
@@ -371,62 +381,75 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   const double ZD = fin < 0 ? 1.0 : __ull2double_rn(st[K + 1 + fin].Z);
   const unsigned long long ZTi = __double2ull_rn(ZT), ZDi = __double2ull_rn(ZD);  // exact: integer values
   constexpr int EPV = E::kEPV;
+  constexpr int NW = kSpecNT / 32;
+  constexpr int TE = kSpecNT * EPV;
+  const int lane = t & 31, warp = t >> 5;
   const int c0 = min(V, rank * a.chunk), c1 = min(V, c0 + a.chunk);
-  // a whole number of 16-byte vectors per thread (c0 is a multiple of 8)
-  const int sub = ((c1 - c0 + kSpecNT - 1) / kSpecNT + EPV - 1) / EPV * EPV;
-  const int v0 = min(c1, c0 + t * sub), v1 = min(c1, v0 + sub);
+  const int n = c1 - c0;
+  const int ntile = (n + TE - 1) / TE;
+  extern __shared__ unsigned long long vtab[];  // [ntile * NW] target sums, then residual sums
   const uint32_t* msk = !kMask ? nullptr : spec_mask(a, b, pos);
-  auto ld = [&](const char* row, int v) { return (msk && !mask_allows(msk, v)) ? neg_inf() : E::load(row, v); };
+  // c0 is a multiple of 8 elements: the slice starts on a 16-byte boundary
+  // whenever the row does
+  const bool vec = ((reinterpret_cast<uintptr_t>(trow) | reinterpret_cast<uintptr_t>(drow)) & 15u) == 0;
+  // elements i0 .. i0 + EPV - 1 of the slice; -inf past its end or where masked
+  auto load_epv = [&](const char* row, int i0, float* x) {
+    if (vec && i0 + EPV <= n) {
+      E::unpack(__ldg(reinterpret_cast<const uint4*>(row + static_cast<int64_t>(c0 + i0) * E::kSize)), x);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPV; e++) x[e] = i0 + e < n ? E::load(row, c0 + i0 + e) : neg_inf();
+    }
+    if (msk) {
+#pragma unroll
+      for (int e = 0; e < EPV; e++)
+        if (i0 + e < n && !mask_allows(msk, c0 + i0 + e)) x[e] = neg_inf();
+    }
+  };
   // every d = x / T - max(x / T) <= 0: the branch-free exact mass applies
-  auto qt_of = [&](int v) { return qmass_le0(__fsub_rn(__fdiv_rn(ld(trow, v), T), smT)); };
-  auto rq_of = [&](int v) {
-    const unsigned long long qd = qmass_le0(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
-    return resid_mass_x(qt_of(v), ZT, ZTi, qd, ZD, ZDi);
+  auto qmT = [&](float x) { return qmass_le0(__fsub_rn(__fdiv_rn(x, T), smT)); };
+  auto qmD = [&](float x) { return qmass_le0(__fsub_rn(__fdiv_rn(x, T), smD)); };
+  auto wsum = [&](unsigned long long w) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(kFull, w, o);
+    return w;
   };
   unsigned long long sT = 0, sR = 0;
-  int vs = v0;  // first element of the scalar rest
-  // unmasked rows on 16-byte boundaries: the thread's run as vectors (the run is
-  // contiguous, so the lines a load misses are the next loads' L1 hits)
-  const bool vec = !kMask && v1 > v0 &&
-                   ((reinterpret_cast<uintptr_t>(trow) | reinterpret_cast<uintptr_t>(drow)) & 15u) == 0;
-  if (vec) {
-    const int nvv = (v1 - v0) / EPV;
-    const uint4* tv = reinterpret_cast<const uint4*>(trow + static_cast<int64_t>(v0) * E::kSize);
-    const uint4* dv = fin >= 0 ? reinterpret_cast<const uint4*>(drow + static_cast<int64_t>(v0) * E::kSize) : nullptr;
-    for (int j = 0; j < nvv; j++) {
-      float xt[EPV];
-      E::unpack(__ldg(tv + j), xt);
-      if (fin >= 0) {
-        float xd[EPV];
-        E::unpack(__ldg(dv + j), xd);
+  for (int tile = 0; tile < ntile; tile++) {
+    const int i0 = tile * TE + t * EPV;
+    float xt[EPV];
+    load_epv(trow, i0, xt);
+    unsigned long long wt = 0, wr = 0;
+    if (fin >= 0) {
+      float xd[EPV];
+      load_epv(drow, i0, xd);
 #pragma unroll
-        for (int e = 0; e < EPV; e++) {
-          const unsigned long long qt = qmass_le0(__fsub_rn(__fdiv_rn(xt[e], T), smT));
-          const unsigned long long qd = qmass_le0(__fsub_rn(__fdiv_rn(xd[e], T), smD));
-          sT += qt;
-          sR += resid_mass_x(qt, ZT, ZTi, qd, ZD, ZDi);
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPV; e++) sT += qmass_le0(__fsub_rn(__fdiv_rn(xt[e], T), smT));
+      for (int e = 0; e < EPV; e++) {
+        const unsigned long long qt = qmT(xt[e]);
+        wt += qt;
+        wr += resid_mass_x(qt, ZT, ZTi, qmD(xd[e]), ZD, ZDi);
       }
+      wr = wsum(wr);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPV; e++) wt += qmT(xt[e]);
     }
-    vs = v0 + nvv * EPV;
-  }
-  if (fin >= 0) {
-    for (int v = vs; v < v1; v++) {
-      const unsigned long long qt = qt_of(v);
-      const unsigned long long qd = qmass_le0(__fsub_rn(__fdiv_rn(ld(drow, v), T), smD));
-      sT += qt;
-      sR += resid_mass_x(qt, ZT, ZTi, qd, ZD, ZDi);
+    wt = wsum(wt);
+    sT += wt;
+    sR += wr;
+    if (lane == 0) {
+      vtab[tile * NW + warp] = wt;
+      vtab[(ntile + tile) * NW + warp] = wr;
     }
-  } else {
-    for (int v = vs; v < v1; v++) sT += qt_of(v);
   }
-  unsigned long long ctaT, ctaR;
-  const unsigned long long befT = block_excl_scan<kSpecNT>(sT, ctaT, sm);
-  const unsigned long long befR = block_excl_scan<kSpecNT>(sR, ctaR, sm);
-  if (t == 0) { c_sumT = ctaT; c_sumR = ctaR; }
+  if (lane == 0) { sm.red_u64[warp] = sT; sm.red_u64[NW + warp] = sR; }
+  __syncthreads();
+  if (t == 0) {
+    unsigned long long cT = 0, cR = 0;
+    for (int w = 0; w < NW; w++) { cT += sm.red_u64[w]; cR += sm.red_u64[NW + w]; }
+    c_sumT = cT;
+    c_sumR = cR;
+  }
   cluster.sync();
   unsigned long long totT = 0, totR = 0, preT = 0, preR = 0;
   for (int q = 0; q < kSpecCluster; q++) {
@@ -438,19 +461,56 @@ __global__ void __cluster_dims__(kSpecCluster, 1, 1) __launch_bounds__(kSpecNT)
   }
   const bool use_resid = fin >= 0 && __dmul_rn(__ull2double_rn(totR), 1.0 / kResidScale) > 1e-10;
   const unsigned long long total = use_resid ? totR : totT;
-  const unsigned long long mine = use_resid ? sR : sT;
-  const unsigned long long before = (use_resid ? preR + befR : preT + befT);
+  const unsigned long long mine = use_resid ? *cluster.map_shared_rank(&c_sumR, rank) : *cluster.map_shared_rank(&c_sumT, rank);
+  const unsigned long long before = use_resid ? preR : preT;
   const unsigned long long rpt = draw_point(a.u_draw[b], total);
   if (total == 0 && rank == 0 && t == 0) a.out_n[b] = n0;  // masked away entirely: no token
-  if (mine > 0 && before <= rpt && rpt < before + mine) {
-    unsigned long long c = before;
-    int pick = v1 - 1;
-    for (int v = v0; v < v1; v++) {
-      c += use_resid ? rq_of(v) : qt_of(v);
-      if (c > rpt) { pick = v; break; }
+  if (mine > 0 && before <= rpt && rpt < before + mine) {  // CTA-uniform
+    // the (tile, warp) entry holding the draw point, in index order
+    const unsigned long long* tab = vtab + (use_resid ? ntile * NW : 0);
+    if (t == 0) {
+      unsigned long long c = before;
+      int ent = ntile * NW - 1;
+      for (int i = 0; i < ntile * NW; i++) {
+        if (rpt < c + tab[i]) { ent = i; break; }
+        c += tab[i];
+      }
+      s_ent = ent;
+      s_before = c;
     }
-    out[n0] = pick;
-    a.out_n[b] = n0 + 1;
+    __syncthreads();
+    const int ent = s_ent;
+    if (warp == ent % NW) {
+      const int i0 = (ent / NW) * TE + t * EPV;
+      float xt[EPV], xd[EPV];
+      unsigned long long q8[EPV], w = 0;
+      load_epv(trow, i0, xt);
+      if (use_resid) load_epv(drow, i0, xd);
+#pragma unroll
+      for (int e = 0; e < EPV; e++) {
+        const unsigned long long qt = qmT(xt[e]);
+        q8[e] = use_resid ? resid_mass_x(qt, ZT, ZTi, qmD(xd[e]), ZD, ZDi) : qt;
+        w += q8[e];
+      }
+      unsigned long long incl = w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long v = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const unsigned long long r2 = rpt - s_before;
+      if (w > 0 && r2 >= incl - w && r2 < incl) {
+        unsigned long long c = incl - w;
+        int pick = c0 + i0 + EPV - 1;
+#pragma unroll
+        for (int e = 0; e < EPV; e++) {
+          c += q8[e];
+          if (c > r2) { pick = c0 + i0 + e; break; }
+        }
+        out[n0] = pick;
+        a.out_n[b] = n0 + 1;
+      }
+    }
   }
   cluster.sync();  // keep this CTA's shared memory alive for its peers
 }
@@ -501,7 +561,10 @@ inline cudaError_t launch_spec_t(SpecArgs a, cudaStream_t st) {
     if (e == cudaSuccess)
       e = spec_launch(spec_stats_kernel<DT, kMask>, a.batch * kSpecCluster, kSpecNT, stage, st, a);
   }
-  if (e == cudaSuccess) e = spec_launch(spec_verify_kernel<DT, kMask>, a.batch * kSpecCluster, kSpecNT, 0, st, a);
+  // the verify kernel's table: two sums per (tile, warp) of a slice
+  const int vtiles = (chunk + kSpecNT * Elt<DT>::kEPV - 1) / (kSpecNT * Elt<DT>::kEPV);
+  const size_t vsmem = static_cast<size_t>(2 * vtiles * (kSpecNT / 32)) * sizeof(unsigned long long);
+  if (e == cudaSuccess) e = spec_launch(spec_verify_kernel<DT, kMask>, a.batch * kSpecCluster, kSpecNT, vsmem, st, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -817,6 +817,16 @@ int32_t tg_debug_phase_cycles(uint64_t* out, int32_t reset) {
   }
   return TG_OK;
 }
+// per-row phase cycles of rows 0..255 (256 x 16), diagnostic builds only
+int32_t tg_debug_row_phases(uint64_t* out, int32_t reset) {
+  TG_CUDA(cudaDeviceSynchronize());
+  TG_CUDA(cudaMemcpyFromSymbol(out, tg::g_row_phase, sizeof(uint64_t) * 256 * 16));
+  if (reset) {
+    static const uint64_t z[256 * 16] = {};
+    TG_CUDA(cudaMemcpyToSymbol(tg::g_row_phase, z, sizeof(z)));
+  }
+  return TG_OK;
+}
 #endif
 
 int32_t tg_sampler_device_status(tg_sampler* s, uint32_t* out_bits) {
