@@ -1746,8 +1746,11 @@ __global__ void __launch_bounds__(NT, kStream ? kStreamCtasPerSm : (kMinCtasPerS
 // entry i; the grid covers every row of the call, and CTAs past the count exit
 // at once.  (A grid-stride loop over a few CTAs per SM spilled five times as
 // much and made rows without top-k 1.4-1.7x slower.)
+#ifndef TG_LIST_MINB
+#define TG_LIST_MINB TG_MIN_CTAS
+#endif
 template <int DT>
-__global__ void __launch_bounds__(kSampleNT, kMinCtasPerSm) sample_list_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(kSampleNT, TG_LIST_MINB) sample_list_kernel(SampleArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the finisher's list (programmatic launch)
   if (static_cast<int>(blockIdx.x) >= *a.fb_count) return;
   sample_row<DT, false, kSampleNT>(a, a.fb_rows[blockIdx.x]);
