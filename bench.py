@@ -350,7 +350,7 @@ def vocab_sharded_leg(torch, dist, s_full, dev, rank, world, local, args, steps=
 
 
 def batch_8192_leg(torch, dev, local, args, steps=20):
-    """Config 4 at its larger batch (8192 rows: two launch pairs of 4096)."""
+    """Config 4 at its larger batch (8192 rows: four launch pairs of 2048)."""
     from tinygpt_b200.sampler import Sampler, params_to_device
     Bb = 8192
     w = make_inputs_gpu(torch, dev, 8192, B=Bb)

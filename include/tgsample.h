@@ -98,8 +98,8 @@ const char* tg_last_error_string(void);
  * at most `max_batch` rows per call.  Allocates the device scratch and the host
  * staging used by the *_host variants; when vocab > 2816 and max_batch >= 1024
  * also the candidate buffer of the two-kernel mode (used for calls of 1024 rows
- * or more), min(max_batch, 4096) rows of
- * 22,536 bytes (92 MB at 4096 rows; environment TG_SAMPLE_SPLIT=0 at creation
+ * or more), min(max_batch, 2048) rows of
+ * 22,536 bytes (46 MB at 2048 rows; environment TG_SAMPLE_SPLIT=0 at creation
  * turns the mode and the buffer off).  Replaces tg_model_create's role as the
  * owner of sampling state (wasm/src/model.h:21-23); returns TG_OK and *out. */
 int32_t tg_sampler_create(int32_t device, int32_t vocab, int32_t max_batch,

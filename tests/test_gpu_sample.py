@@ -267,7 +267,7 @@ def test_full_row_stages_without_topk(oracle_mod, sampler_factory, V, dtype, B):
 
 def test_config4_batch_8192(oracle_mod, sampler_factory):
     """Config 4 at its larger batch ("batch 2048 (also
-    8192)"): two streaming / finishing launch pairs of 4096 rows each."""
+    8192)"): four streaming / finishing launch pairs of 2048 rows each."""
     w = W.make(4, seed=7, batch=8192)
     s = sampler_factory(w["vocab"], max_batch=8192)
     assert_same(oracle_mod, s, w, what="config 4 B=8192")

@@ -154,7 +154,7 @@ cudaError_t launch_dependent(void (*kernel)(KArgs...), int grid, int block, size
 
 // Rows per streaming / finishing launch pair (bounds the candidate buffer:
 // kCandMax * 8 + 8 bytes per row).
-constexpr int kSplitRows = 4096;
+constexpr int kSplitRows = 2048;
 // The two-kernel mode pays for itself from this many rows on.
 constexpr int kSplitMinBatchDefault = 1024;
 // TG_SPLIT_MIN_BATCH overrides it (diagnostics: the two-kernel mode on small batches).
