@@ -20,8 +20,16 @@ constexpr double kResidScale = 4503599627370496.0;  // 2^52: scale of residual m
 // or two multiplications by powers of two.  Accuracy < 1 ulp over the normal
 // range (checked against libm in the tests).  Independent of CUDA's expf.
 // The reduction and the polynomial: x = n*ln2 + r, p = e^r.
+// n = rint(x * log2(e)) without the conversion pipe: for |p| < 2^22, adding
+// 1.5 * 2^23 puts p + 1.5 * 2^23 in [2^23, 2^24), where the spacing of floats is
+// 1, so the correctly rounded sum is p rounded to an integer, ties to even (the
+// constant is even), exactly rintf(p); its bits minus the constant's bits are
+// that integer.  Every x used here gives |p| < 151 (tg_exp returns early
+// outside (-104, 88]; qmass_le0 discards d < -32, whatever ni is then).
 __device__ __forceinline__ float tg_exp_poly(float x, int& ni) {
-  const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23, bits 0x4B400000
+  const float tr = __fadd_rn(__fmul_rn(x, 1.44269504088896341f), kRound);
+  const float n = __fsub_rn(tr, kRound);
   float r = __fmaf_rn(n, -0.693145751953125f, x);
   r = __fmaf_rn(n, -1.42860676533018e-06f, r);
   float p = 1.98412698412698e-04f;
@@ -32,7 +40,7 @@ __device__ __forceinline__ float tg_exp_poly(float x, int& ni) {
   p = __fmaf_rn(p, r, 0.5f);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
-  ni = __float2int_rn(n);
+  ni = __float_as_int(tr) - 0x4B400000;
   return p;
 }
 
@@ -53,13 +61,14 @@ __device__ __forceinline__ uint64_t qmass(float d) {
 }
 
 // qmass(d) for d <= 0 without branches: for -32 <= d <= 0 tg_exp takes its
-// first scaling branch (n >= -47), so the same operations give the same bits;
-// below -32 (or NaN) the select gives 0.
+// first scaling branch (n >= -47), and both of qmass's scalings (by 2^n, then
+// by 2^44) are exact there (normal results), so one multiplication by
+// 2^(n + 44) gives the same bits; below -32 (or NaN) the select gives 0.
 __device__ __forceinline__ uint64_t qmass_le0(float d) {
   int ni;
   const float p = tg_exp_poly(d, ni);
-  const float e = __fmul_rn(p, __uint_as_float((static_cast<uint32_t>(ni) + 127u) << 23));
-  const uint64_t q = __float2ull_rz(__fmul_rn(e, kMassScale));
+  const float e44 = __fmul_rn(p, __uint_as_float((static_cast<uint32_t>(ni) + 171u) << 23));
+  const uint64_t q = __float2ull_rz(e44);
   return d >= -32.0f ? q : 0ull;
 }
 
