@@ -56,3 +56,22 @@ def test_spec_mixed_modes(oracle_mod, sampler_factory, dtype):
                                     w["u_accept"], w["u_draw"])
     assert np.array_equal(n, on)
     assert np.array_equal(o, oo)
+
+
+@pytest.mark.parametrize("V,dtype", [(128256, "bf16"), (50257, "f32"), (50257, "bf16"), (32000, "bf16")])
+def test_spec_vocab_shapes(oracle_mod, sampler_factory, V, dtype):
+    """Config-5 rows at the configurations' vocabularies, f32 and bf16: whole and
+    partial tiles of the draw pass, rows on and off 16-byte boundaries
+    (V=50257 in f32 or bf16 leaves every row but the first unaligned)."""
+    B = 32
+    w = W.make(5, seed=11, batch=B, vocab=V)
+    w["temperature"][::6] = 0.0  # some greedy rows
+    if dtype == "bf16":  # the oracle sees the same bf16 values
+        w["target"] = W.bf16_bits_to_f32(W.to_bf16_bits(w["target"]))
+        w["draft"] = W.bf16_bits_to_f32(W.to_bf16_bits(w["draft"]))
+    s = sampler_factory(V)
+    o, n = run(s, w, dtype)
+    oo, on = oracle_mod.spec_verify(w["target"], w["draft"], w["draft_ids"], w["temperature"],
+                                    w["u_accept"], w["u_draw"])
+    assert np.array_equal(n, on)
+    assert np.array_equal(o, oo)
