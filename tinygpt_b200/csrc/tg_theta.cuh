@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(kThetaNT) theta_kernel(SampleArgs a) {
   const bool greedy = !(p.temperature > 0.0f);
   const bool topk = p.top_k > 0 && p.top_k < V;
   const int keff = greedy ? 1 : (topk ? p.top_k : V);
-  const float tgt = kTgtMul * static_cast<float>(keff < V ? keff : kNoTopkTarget) + kTgtAdd;
+  const float tgt = kTgtMul * static_cast<float>(keff < V ? keff : kNoTopkTargetStream) + kTgtAdd;  // feeds the stream
   const int nsv = nvec < kSampleVecs * kSampleNT ? nvec : kSampleVecs * kSampleNT;
   const int sampled = nsv * EPV;
   if (!(V > kCandMax && sampled > 0)) {
