@@ -41,10 +41,11 @@ constexpr int kSampleVecs = 4;   // 128-bit vectors per thread in the threshold 
 #endif
 constexpr int kUnroll = TG_UNROLL;  // 128-bit loads in flight per thread
 constexpr int kNoTopkTarget = 512;  // candidate target of rows without top-k
-// ... in the streaming kernel of the two-kernel mode: a longer list holds the
-// top-p cut more often, so fewer rows fail their list and re-stream (config-4
-// rows without top-k 2822 -> 2523 us); the CTA-per-row kernels keep 512
-// (config 2 took 49 -> 144 us with 1024)
+// ... in the streaming kernel and the 256-thread CTA-per-row kernels: a longer
+// list holds the top-p cut more often, so fewer rows fail their list and
+// re-stream (config-4 rows without top-k 2822 -> 2523 us with the stream alone);
+// the 1024-thread kernel of small batches keeps 512 (config 2 took 49 -> 144 us
+// with 1024)
 constexpr int kNoTopkTargetStream = 1024;
 constexpr int kRetries = 2;      // threshold retries (re-streamed from L2) before the full row
 #ifndef TG_MIN_CTAS
@@ -1245,7 +1246,8 @@ __device__ __forceinline__ void sample_row(const SampleArgs& a, const int b) {
     const int keff = greedy ? 1 : (topk ? p.top_k : V);
     const unsigned int need = static_cast<unsigned int>(keff < V ? keff : 1);
     const float tgt =
-        kTgtMul * static_cast<float>(keff < V ? keff : (kStream ? kNoTopkTargetStream : kNoTopkTarget)) + kTgtAdd;
+        kTgtMul * static_cast<float>(keff < V ? keff : (kStream || NT == kSampleNT ? kNoTopkTargetStream : kNoTopkTarget)) +
+        kTgtAdd;
     const int lane = t & 31, warp = t >> 5;
     const unsigned lt = (1u << lane) - 1u;
 
